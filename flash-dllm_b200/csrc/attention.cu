@@ -1,0 +1,741 @@
+// Block-table scheduled attention over the KV cache (Flash-Cache) and the
+// Flash-Verify attention, as one warp-specialised kernel template.
+//
+// Work item = up to 64 query rows of one sequence x one head x one slice of
+// that sequence's keys.  For Flash-Cache an item holds the sequence's masked
+// rows first and then its tracked (refresh) rows, so masked and tracked rows
+// share one pass over K/V (the reference runs two kernels, two passes).
+//
+// CTA = 5 warps.  Warp 4 is the producer: it stages 64-key K and V tiles
+// (128-byte-swizzled rows, 2 x 8 KB halves per tile) into a 3-deep smem ring --
+// with TMA box loads for contiguous cache ranges, or with 16-byte cp.async
+// gathers (zero-filling invalid keys) for the verify key list and the verify
+// block's own K/V.  Warps 0-3 each own 16 query rows: Q fragments stay in
+// registers, S = Q K^T and O += P V run on mma.sync m16n8k16 (bf16 in, fp32
+// accumulate) with ldmatrix from the swizzled tiles, P never leaves
+// registers, and the online softmax works in the exp2 domain.  When masked
+// rows are present the raw (unscaled) logits of those rows are summed per
+// key across the warp and added to attn_scores (the reference's S tensor and
+// S.mean((0,1)) fused into one atomic per key, warp and head).
+#include <cstring>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace fdllm {
+
+constexpr int kHD = 128;
+constexpr int kItemRows = 64;
+constexpr int kKeyTile = 64;
+constexpr int kAttnStages = 3;
+constexpr int kComputeWarps = 4;
+constexpr int kAttnThreads = (kComputeWarps + 1) * 32;
+constexpr int kHalfBytes = kKeyTile * 128;          // 64 rows x 128 B (64 dims)
+constexpr int kTileBytes = 2 * kHalfBytes;          // one K or V tile (128 dims)
+constexpr int kAttnStageBytes = 2 * kTileBytes;     // K + V
+constexpr int kAttnBarOffset = kAttnStages * kAttnStageBytes;
+constexpr int kAttnSmem = 1024 + kAttnBarOffset + 128;
+constexpr int kPlanHeader = 8;
+constexpr int kPlanItem = 8;
+constexpr int kAttnKernelId = 2;
+constexpr int kPlanKernelId = 3;
+
+// Byte offset of 16-byte chunk `chunk` (0..15, 8 dims each) of key row `row`
+// inside a tile stored as two 64-dim halves with the 128-byte swizzle -- the
+// layout a SWIZZLE_128B TMA box of {64 dims, 64 rows} produces.
+__device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
+  return (chunk >> 3) * kHalfBytes + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// 16-byte async copy; with valid == false nothing is read and 16 zero bytes land.
+__device__ __forceinline__ void cp_async_16_zfill(void* smem_dst, const void* gmem_src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+
+struct AttnParams {
+  const __nv_bfloat16* q;
+  __nv_bfloat16* o;
+  const __nv_bfloat16* kc;      // cache K
+  const __nv_bfloat16* vc;      // cache V
+  const __nv_bfloat16* k1;      // verify: fresh K/V of the verify rows (row-indexed)
+  const __nv_bfloat16* v1;
+  const int32_t* plan;          // cache mode: plan from fdllm_plan_cache_attention
+  const int32_t* vblocks;       // verify mode: (k_s, k_e, q_s, q_e) rows
+  const int64_t* pos_k;         // verify mode: gathered key slots
+  const uint8_t* mask;          // verify mode: [n_blocks*block_rows, block_rows]
+  float* scores;                // cache mode, optional
+  float* part_o;                // split-KV partials [item][head][split][64][128]
+  float* part_ml;               // [item][head][split][64][2]
+  int32_t* status;
+  int64_t n_slots;
+  int64_t n_pos_k;
+  float scale_log2;             // softmax_scale * log2(e)
+  float score_scale;
+  int32_t d_model;
+  int32_t n_heads;
+  int32_t seqlen_max;
+  int32_t kv_splits;
+  int32_t n_items;              // verify mode: n_blocks * row chunks
+  int32_t block_rows;           // verify mode
+  int32_t row_chunks;           // verify mode: ceil(block_rows / 64)
+  int32_t n_rows;               // rows of q / o (and of k1 / v1 in verify mode)
+};
+
+// Item description resolved by every thread of the CTA.
+struct Item {
+  int seq;          // cache mode: sequence slot; verify mode: verify block index
+  int n_keys;       // keys of the cache part (contiguous range or gathered list)
+  int k_base;       // verify: offset into pos_k
+  int rows;         // query rows in this item (<= 64)
+  int m_start, m_len, t_start;   // row segments: [m_start, +m_len) then [t_start, ...)
+  int blk_rows;     // verify: rows of the block, also its in-block key count
+  int blk_q0;       // verify: first row of the block (q_s)
+  int chunk_row0;   // verify: first block row of this item (64 * chunk)
+};
+
+__device__ __forceinline__ int item_row(const Item& it, int r) {
+  return r < it.m_len ? it.m_start + r : it.t_start + (r - it.m_len);
+}
+
+__device__ __forceinline__ bool load_item(const AttnParams& p, bool verify, int item_id, Item& it) {
+  if (!verify) {
+    if (item_id >= p.plan[0]) return false;
+    const int32_t* e = p.plan + kPlanHeader + item_id * kPlanItem;
+    it.seq = e[0];
+    it.n_keys = e[1];
+    it.m_start = e[2];
+    it.m_len = e[3];
+    it.t_start = e[4];
+    it.rows = e[3] + e[5];
+    return it.rows > 0;
+  }
+  if (item_id >= p.n_items) return false;
+  const int b = item_id / p.row_chunks;
+  const int c = item_id % p.row_chunks;
+  const int32_t* r = p.vblocks + 4 * b;
+  const int k_s = r[0], k_e = r[1], q_s = r[2];
+  const int q_e = min(r[3], p.n_rows);  // rows past the query tensors are never read
+  if (q_s < 0 || r[3] > p.n_rows || k_s < 0) {
+    if (c == 0) report(p.status, FDLLM_ERR_TABLE, b, kAttnKernelId);
+    return false;
+  }
+  it.seq = b;
+  it.k_base = k_s;
+  it.n_keys = max(0, k_e - k_s);
+  it.blk_q0 = q_s;
+  it.blk_rows = max(0, min(q_e - q_s, p.block_rows));
+  it.chunk_row0 = c * kItemRows;
+  it.m_start = q_s + c * kItemRows;
+  it.m_len = max(0, min(kItemRows, it.blk_rows - c * kItemRows));
+  it.t_start = 0;
+  it.rows = it.m_len;
+  return it.rows > 0;
+}
+
+template <bool kVerify>
+__global__ void __launch_bounds__(kAttnThreads, 2)
+    attn_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kAttnBarOffset);
+  uint64_t* empty = full + kAttnStages;
+  int32_t* sflag = reinterpret_cast<int32_t*>(empty + kAttnStages);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int item_id = blockIdx.x;
+  const int head = blockIdx.y;
+  const int split = blockIdx.z;
+
+  Item it{};
+  if (!load_item(p, kVerify, item_id, it)) return;  // uniform across the CTA
+  // keys of this split: equal 64-aligned slices of the item's key range
+  const int per = ((it.n_keys + p.kv_splits - 1) / p.kv_splits + kKeyTile - 1) / kKeyTile * kKeyTile;
+  const int c0 = min(it.n_keys, split * per);
+  const int c1 = min(it.n_keys, c0 + per);
+  const int nt_cache = (c1 - c0 + kKeyTile - 1) / kKeyTile;
+  const bool last_split = split == p.kv_splits - 1;
+  const int nt_blk = (kVerify && last_split) ? (it.blk_rows + kKeyTile - 1) / kKeyTile : 0;
+  const int n_tiles = nt_cache + nt_blk;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kAttnStages; ++s) {
+      mbar_init(&full[s], kVerify ? 32 : 1);
+      mbar_init(&empty[s], kComputeWarps);
+    }
+    sflag[0] = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int64_t d = p.d_model;
+  if (warp == kComputeWarps) {
+    // -------------------------------------------------------- producer ----
+    for (int t = 0; t < n_tiles; ++t) {
+      const int s = t % kAttnStages;
+      const uint32_t ph = (t / kAttnStages) & 1;
+      if (t >= kAttnStages && !mbar_wait(&empty[s], ph ^ 1, p.status, kAttnKernelId)) break;
+      uint8_t* kt = smem + s * kAttnStageBytes;
+      uint8_t* vt = kt + kTileBytes;
+      if (!kVerify) {
+        if (lane == 0) {
+          const int y = it.seq * p.seqlen_max + c0 + t * kKeyTile;
+          mbar_arrive_expect_tx(&full[s], kAttnStageBytes);
+          tma_load_2d(kt, &map_k, head * kHD, y, &full[s]);
+          tma_load_2d(kt + kHalfBytes, &map_k, head * kHD + 64, y, &full[s]);
+          tma_load_2d(vt, &map_v, head * kHD, y, &full[s]);
+          tma_load_2d(vt + kHalfBytes, &map_v, head * kHD + 64, y, &full[s]);
+        }
+      } else {
+        const bool blk = t >= nt_cache;
+        const int n0 = blk ? (t - nt_cache) * kKeyTile : c0 + t * kKeyTile;
+        const int n_end = blk ? it.blk_rows : c1;
+        // lane covers 16-byte chunk (lane % 16) of keys (lane / 16) + 2i
+#pragma unroll 4
+        for (int i = 0; i < kKeyTile / 2; ++i) {
+          const int key = 2 * i + (lane >> 4);
+          const int chunk = lane & 15;
+          const int n = n0 + key;
+          bool valid = n < n_end;
+          const __nv_bfloat16* ksrc = p.kc;
+          const __nv_bfloat16* vsrc = p.vc;
+          if (valid) {
+            if (blk) {
+              const int64_t row = it.blk_q0 + n;
+              ksrc = p.k1 + row * d + head * kHD + chunk * 8;
+              vsrc = p.v1 + row * d + head * kHD + chunk * 8;
+            } else {
+              const int64_t pk = static_cast<int64_t>(it.k_base) + n;
+              const int64_t row = (pk < p.n_pos_k) ? p.pos_k[pk] : -1;
+              if (row < 0 || row >= p.n_slots) {
+                report(p.status, FDLLM_ERR_INDEX, static_cast<int>(pk), kAttnKernelId);
+                valid = false;
+              } else {
+                ksrc = p.kc + row * d + head * kHD + chunk * 8;
+                vsrc = p.vc + row * d + head * kHD + chunk * 8;
+              }
+            }
+          }
+          cp_async_16_zfill(kt + tile_off(key, chunk), ksrc, valid);
+          cp_async_16_zfill(vt + tile_off(key, chunk), vsrc, valid);
+        }
+        cp_async_mbar_arrive(&full[s]);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ compute ----
+  const int g = lane >> 2;
+  const int tq = lane & 3;
+  const int r0 = warp * 16 + g;      // item rows of this thread: r0, r0 + 8
+  const int r1 = r0 + 8;
+  const bool v0 = r0 < it.rows, v1 = r1 < it.rows;
+  const int64_t grow0 = v0 ? item_row(it, r0) : 0;
+  const int64_t grow1 = v1 ? item_row(it, r1) : 0;
+  const bool score_rows = (!kVerify) && p.scores != nullptr && (warp * 16 < it.m_len);
+  const float mrow0 = (!kVerify && r0 < it.m_len) ? 1.f : 0.f;
+  const float mrow1 = (!kVerify && r1 < it.m_len) ? 1.f : 0.f;
+
+  // Q fragments (A operand, 16 rows x 128 dims) straight from global memory.
+  uint32_t qa[8][4];
+  {
+    const uint32_t* q0p = reinterpret_cast<const uint32_t*>(p.q + grow0 * d + head * kHD);
+    const uint32_t* q1p = reinterpret_cast<const uint32_t*>(p.q + grow1 * d + head * kHD);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      qa[kk][0] = v0 ? __ldg(q0p + kk * 8 + tq) : 0u;
+      qa[kk][1] = v1 ? __ldg(q1p + kk * 8 + tq) : 0u;
+      qa[kk][2] = v0 ? __ldg(q0p + kk * 8 + 4 + tq) : 0u;
+      qa[kk][3] = v1 ? __ldg(q1p + kk * 8 + 4 + tq) : 0u;
+    }
+  }
+
+  float oacc[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const uint8_t* mrow_ptr0 = nullptr;
+  const uint8_t* mrow_ptr1 = nullptr;
+  if (kVerify) {
+    const int64_t base = static_cast<int64_t>(it.seq) * p.block_rows + it.chunk_row0;
+    mrow_ptr0 = p.mask + (base + min(r0, it.rows - 1)) * p.block_rows;
+    mrow_ptr1 = p.mask + (base + min(r1, it.rows - 1)) * p.block_rows;
+  }
+
+  for (int t = 0; t < n_tiles; ++t) {
+    const int s = t % kAttnStages;
+    const uint32_t ph = (t / kAttnStages) & 1;
+    const bool got = mbar_wait(&full[s], ph, p.status, kAttnKernelId);
+    const bool blk = kVerify && t >= nt_cache;
+    const int n0 = blk ? (t - nt_cache) * kKeyTile : c0 + t * kKeyTile;
+    const int n_valid = (blk ? it.blk_rows : c1) - n0;   // keys of this tile that exist
+    uint8_t* kt = smem + s * kAttnStageBytes;
+    uint8_t* vt = kt + kTileBytes;
+    if (!kVerify && n_valid < kKeyTile) {
+      // TMA brought whole rows past the end of this key range: zero their V so
+      // 0-probability keys cannot inject non-finite cache contents.  Every
+      // compute warp reaches both barriers, including one whose wait ran out.
+      if (!got) sflag[0] = 1;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (sflag[0] == 0) {
+        for (int idx = threadIdx.x; idx < (kKeyTile - n_valid) * 16; idx += 128) {
+          const int key = n_valid + idx / 16, chunk = idx % 16;
+          *reinterpret_cast<uint4*>(vt + tile_off(key, chunk)) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (sflag[0] != 0) return;
+    }
+    if (!got) return;
+    const uint32_t kbase = smem_u32(kt), vbase = smem_u32(vt);
+
+    // S = Q K^T  (16 rows x 64 keys per warp)
+    float sacc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+      for (int jp = 0; jp < 4; ++jp) {
+        const int mi = lane >> 3;
+        const int key = jp * 16 + (mi >> 1) * 8 + (lane & 7);
+        const int chunk = 2 * kk + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kbase + tile_off(key, chunk), b0, b1, b2, b3);
+        mma_bf16(sacc[2 * jp], qa[kk], b0, b1);
+        mma_bf16(sacc[2 * jp + 1], qa[kk], b2, b3);
+      }
+    }
+
+    // key validity (+ verify in-block mask), raw-score accumulation
+    float colsum[8][2];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int kl = j * 8 + 2 * tq + e;
+        const bool kv_ok = kl < n_valid;
+        bool ok0 = kv_ok, ok1 = kv_ok;
+        if (blk) {
+          const int kj = n0 + kl;
+          ok0 = ok0 && mrow_ptr0[kj] != 0;
+          ok1 = ok1 && mrow_ptr1[kj] != 0;
+        }
+        colsum[j][e] = kv_ok ? (sacc[j][e] * mrow0 + sacc[j][2 + e] * mrow1) : 0.f;
+        sacc[j][e] = ok0 ? sacc[j][e] * p.scale_log2 : -INFINITY;
+        sacc[j][2 + e] = ok1 ? sacc[j][2 + e] * p.scale_log2 : -INFINITY;
+      }
+    }
+    if (score_rows) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float v = colsum[j][e];
+          v += __shfl_xor_sync(0xffffffffu, v, 4);
+          v += __shfl_xor_sync(0xffffffffu, v, 8);
+          v += __shfl_xor_sync(0xffffffffu, v, 16);
+          colsum[j][e] = v;
+        }
+      }
+      if (g == 0) {
+        float* srow = p.scores + static_cast<int64_t>(it.seq) * p.seqlen_max + n0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int kl = j * 8 + 2 * tq + e;
+            if (kl < n_valid) atomicAdd(srow + kl, colsum[j][e] * p.score_scale);
+          }
+      }
+    }
+
+    // online softmax (exp2 domain)
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      mx0 = fmaxf(mx0, fmaxf(sacc[j][0], sacc[j][1]));
+      mx1 = fmaxf(mx1, fmaxf(sacc[j][2], sacc[j][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float ref0 = mn0 == -INFINITY ? 0.f : mn0;
+    const float ref1 = mn1 == -INFINITY ? 0.f : mn1;
+    const float al0 = exp2f(m0 - ref0), al1 = exp2f(m1 - ref1);
+    m0 = mn0;
+    m1 = mn1;
+    float ps0 = 0.f, ps1 = 0.f;
+    uint32_t pa[4][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float p00 = exp2f(sacc[j][0] - ref0), p01 = exp2f(sacc[j][1] - ref0);
+      const float p10 = exp2f(sacc[j][2] - ref1), p11 = exp2f(sacc[j][3] - ref1);
+      ps0 += p00 + p01;
+      ps1 += p10 + p11;
+      pa[j >> 1][(j & 1) * 2 + 0] = pack_bf16x2(p00, p01);
+      pa[j >> 1][(j & 1) * 2 + 1] = pack_bf16x2(p10, p11);
+    }
+    l0 = l0 * al0 + ps0;
+    l1 = l1 * al1 + ps1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      oacc[j][0] *= al0;
+      oacc[j][1] *= al0;
+      oacc[j][2] *= al1;
+      oacc[j][3] *= al1;
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int jp = 0; jp < 8; ++jp) {
+        const int mi = lane >> 3;
+        const int key = kk * 16 + (mi & 1) * 8 + (lane & 7);
+        const int chunk = 2 * jp + (mi >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vbase + tile_off(key, chunk), b0, b1, b2, b3);
+        mma_bf16(oacc[2 * jp], pa[kk], b0, b1);
+        mma_bf16(oacc[2 * jp + 1], pa[kk], b2, b3);
+      }
+    }
+    if (!kVerify) fence_proxy_async_smem();  // generic zero-fill before the next TMA write
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+  if (p.kv_splits == 1) {
+    const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+    const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+    __nv_bfloat16* o0 = p.o + grow0 * d + head * kHD;
+    __nv_bfloat16* o1 = p.o + grow1 * d + head * kHD;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (v0) *reinterpret_cast<uint32_t*>(o0 + j * 8 + 2 * tq) = pack_bf16x2(oacc[j][0] * inv0, oacc[j][1] * inv0);
+      if (v1) *reinterpret_cast<uint32_t*>(o1 + j * 8 + 2 * tq) = pack_bf16x2(oacc[j][2] * inv1, oacc[j][3] * inv1);
+    }
+  } else {
+    const int64_t slot = (static_cast<int64_t>(item_id) * p.n_heads + head) * p.kv_splits + split;
+    float* po = p.part_o + slot * kItemRows * kHD;
+    float* pml = p.part_ml + slot * kItemRows * 2;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      *reinterpret_cast<float2*>(po + r0 * kHD + j * 8 + 2 * tq) = make_float2(oacc[j][0], oacc[j][1]);
+      *reinterpret_cast<float2*>(po + r1 * kHD + j * 8 + 2 * tq) = make_float2(oacc[j][2], oacc[j][3]);
+    }
+    if (tq == 0) {
+      *reinterpret_cast<float2*>(pml + r0 * 2) = make_float2(m0, l0);
+      *reinterpret_cast<float2*>(pml + r1 * 2) = make_float2(m1, l1);
+    }
+  }
+}
+
+// Merge split-KV partials: O = sum_s 2^(m_s - m) O_s / sum_s 2^(m_s - m) l_s.
+template <bool kVerify>
+__global__ void __launch_bounds__(256) attn_combine_kernel(const AttnParams p) {
+  const int item_id = blockIdx.x;
+  const int head = blockIdx.y;
+  Item it{};
+  if (!load_item(p, kVerify, item_id, it)) return;
+  const int64_t base = (static_cast<int64_t>(item_id) * p.n_heads + head) * p.kv_splits;
+  // work unit: row = w / 4, dims [(w%4)*32, +32)
+  for (int w = threadIdx.x; w < kItemRows * 4; w += blockDim.x) {
+    const int r = w >> 2;
+    if (r >= it.rows) continue;
+    const int d0 = (w & 3) * 32;
+    float mmax = -INFINITY;
+    for (int s = 0; s < p.kv_splits; ++s) mmax = fmaxf(mmax, p.part_ml[((base + s) * kItemRows + r) * 2]);
+    const float ref = mmax == -INFINITY ? 0.f : mmax;
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+    float lsum = 0.f;
+    for (int s = 0; s < p.kv_splits; ++s) {
+      const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + ((base + s) * kItemRows + r) * 2);
+      const float wgt = exp2f(ml.x - ref);
+      lsum += wgt * ml.y;
+      const float* po = p.part_o + ((base + s) * kItemRows + r) * kHD + d0;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(po + i);
+        acc[i] += wgt * v.x;
+        acc[i + 1] += wgt * v.y;
+        acc[i + 2] += wgt * v.z;
+        acc[i + 3] += wgt * v.w;
+      }
+    }
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    __nv_bfloat16* o = p.o + static_cast<int64_t>(item_row(it, r)) * p.d_model + head * kHD + d0;
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+      uint4 v;
+      v.x = pack_bf16x2(acc[i] * inv, acc[i + 1] * inv);
+      v.y = pack_bf16x2(acc[i + 2] * inv, acc[i + 3] * inv);
+      v.z = pack_bf16x2(acc[i + 4] * inv, acc[i + 5] * inv);
+      v.w = pack_bf16x2(acc[i + 6] * inv, acc[i + 7] * inv);
+      *reinterpret_cast<uint4*>(o + i) = v;
+    }
+  }
+}
+
+// ------------------------------------------------------------ planner ----
+constexpr int kPlanThreads = 1024;
+constexpr int kPlanMaxBatch = 1024;
+
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* __restrict__ masked, int n_masked,
+                                                            const int64_t* __restrict__ tracked, int n_tracked,
+                                                            int batch, int block_m, int seqlen_max, int n_rows,
+                                                            int capacity, int32_t* __restrict__ plan,
+                                                            int32_t* status) {
+  __shared__ int m_start[kPlanMaxBatch], m_len[kPlanMaxBatch], m_cnt[kPlanMaxBatch];
+  __shared__ int t_min[kPlanMaxBatch], t_max[kPlanMaxBatch], t_len[kPlanMaxBatch];
+  __shared__ int k_end[kPlanMaxBatch], n_it[kPlanMaxBatch], off[kPlanMaxBatch];
+  __shared__ int bad;
+  const int tid = threadIdx.x;
+  if (tid == 0) bad = 0;
+  for (int b = tid; b < batch; b += kPlanThreads) {
+    m_start[b] = 0;
+    m_len[b] = 0;
+    m_cnt[b] = 0;
+    t_min[b] = INT32_MAX;
+    t_max[b] = -1;
+    t_len[b] = 0;
+    k_end[b] = -1;
+  }
+  __syncthreads();
+  for (int i = tid; i < n_masked + n_tracked; i += kPlanThreads) {
+    const bool is_m = i < n_masked;
+    const int64_t* r = is_m ? masked + 4 * i : tracked + 4 * (i - n_masked);
+    const int64_t b = r[0], ke = r[1], qs = r[2], qe = r[3];
+    if (b < 0 || b >= batch || ke <= 0 || ke > seqlen_max || qs < 0 || qe <= qs || qe - qs > block_m ||
+        qe > n_rows) {
+      atomicExch(&bad, i + 1);
+      continue;
+    }
+    const int prev = atomicCAS(&k_end[b], -1, static_cast<int>(ke));
+    if (prev != -1 && prev != ke) atomicExch(&bad, i + 1);
+    if (is_m) {
+      if (atomicAdd(&m_cnt[b], 1) != 0) atomicExch(&bad, i + 1);
+      m_start[b] = static_cast<int>(qs);
+      m_len[b] = static_cast<int>(qe - qs);
+    } else {
+      atomicMin(&t_min[b], static_cast<int>(qs));
+      atomicMax(&t_max[b], static_cast<int>(qe));
+      atomicAdd(&t_len[b], static_cast<int>(qe - qs));
+    }
+  }
+  __syncthreads();
+  for (int b = tid; b < batch; b += kPlanThreads) {
+    if (t_len[b] > 0 && t_max[b] - t_min[b] != t_len[b]) atomicExch(&bad, n_masked + 1);
+    const int rows = m_len[b] + t_len[b];
+    n_it[b] = rows > 0 ? (rows + kItemRows - 1) / kItemRows : 0;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int b = 0; b < batch; ++b) {
+      off[b] = acc;
+      acc += n_it[b];
+    }
+    if (acc > capacity) bad = -1;
+    plan[0] = bad != 0 ? 0 : acc;
+    if (bad != 0) report(status, FDLLM_ERR_TABLE, bad, kPlanKernelId);
+  }
+  __syncthreads();
+  if (bad != 0) return;
+  for (int b = tid; b < batch; b += kPlanThreads) {
+    const int rows = m_len[b] + t_len[b];
+    for (int k = 0; k < n_it[b]; ++k) {
+      const int v0 = k * kItemRows, v1 = min(rows, v0 + kItemRows);
+      const int mseg = max(0, min(v1, m_len[b]) - v0);
+      const int tfrom = max(v0, m_len[b]);
+      int32_t* e = plan + kPlanHeader + (off[b] + k) * kPlanItem;
+      e[0] = b;
+      e[1] = k_end[b];
+      e[2] = m_start[b] + v0;
+      e[3] = mseg;
+      e[4] = t_len[b] > 0 ? t_min[b] + (tfrom - m_len[b]) : 0;
+      e[5] = max(0, v1 - tfrom);
+      e[6] = 0;
+      e[7] = 0;
+    }
+  }
+}
+
+namespace {
+
+int plan_capacity(int32_t n_rows, int32_t batch) { return (n_rows + kItemRows - 1) / kItemRows + batch; }
+
+size_t attn_ws_bytes(int32_t items, int32_t heads, int32_t splits) {
+  if (splits <= 1) return 256;
+  const size_t slots = static_cast<size_t>(items) * heads * splits;
+  return align_up(slots * kItemRows * kHD * sizeof(float), 256) + slots * kItemRows * 2 * sizeof(float);
+}
+
+template <bool kVerify>
+int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, AttnParams& p, int grid_items, void* ws,
+                size_t ws_bytes, cudaStream_t stream) {
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(attn_kernel<kVerify>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem) !=
+        cudaSuccess)
+      return FDLLM_ERR_CUDA;
+    attr[dev] = true;
+  }
+  if (p.kv_splits > 1) {
+    if (ws == nullptr || ws_bytes < attn_ws_bytes(grid_items, p.n_heads, p.kv_splits)) return FDLLM_ERR_WORKSPACE;
+    const size_t slots = static_cast<size_t>(grid_items) * p.n_heads * p.kv_splits;
+    p.part_o = static_cast<float*>(ws);
+    p.part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) +
+                                         align_up(slots * kItemRows * kHD * sizeof(float), 256));
+  }
+  dim3 grid(grid_items, p.n_heads, p.kv_splits);
+  attn_kernel<kVerify><<<grid, kAttnThreads, kAttnSmem, stream>>>(mk, mv, p);
+  if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
+  if (p.kv_splits > 1) {
+    attn_combine_kernel<kVerify><<<dim3(grid_items, p.n_heads), 256, 0, stream>>>(p);
+    if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
+  }
+  return FDLLM_OK;
+}
+
+}  // namespace
+}  // namespace fdllm
+
+extern "C" {
+
+int fdllm_attn_plan_capacity(int32_t n_rows, int32_t batch_size) {
+  return fdllm::plan_capacity(n_rows < 0 ? 0 : n_rows, batch_size < 0 ? 0 : batch_size);
+}
+
+size_t fdllm_attn_plan_bytes(int32_t n_rows, int32_t batch_size) {
+  const int cap = fdllm_attn_plan_capacity(n_rows, batch_size);
+  return sizeof(int32_t) * (fdllm::kPlanHeader + static_cast<size_t>(cap) * fdllm::kPlanItem);
+}
+
+int fdllm_plan_cache_attention(const int64_t* masked_blocks, int32_t n_masked, const int64_t* tracked_blocks,
+                               int32_t n_tracked, int32_t n_rows, int32_t batch_size, int32_t block_m,
+                               int32_t seqlen_max, void* plan, size_t plan_bytes, cudaStream_t stream) {
+  if (n_masked < 0 || n_tracked < 0 || n_rows < 0 || batch_size <= 0 || batch_size > fdllm::kPlanMaxBatch ||
+      block_m <= 0 || seqlen_max <= 0 || plan == nullptr)
+    return FDLLM_ERR_ARG;
+  if ((n_masked > 0 && masked_blocks == nullptr) || (n_tracked > 0 && tracked_blocks == nullptr))
+    return FDLLM_ERR_ARG;
+  if (plan_bytes < fdllm_attn_plan_bytes(n_rows, batch_size)) return FDLLM_ERR_WORKSPACE;
+  fdllm::plan_kernel<<<1, fdllm::kPlanThreads, 0, stream>>>(
+      masked_blocks, n_masked, tracked_blocks, n_tracked, batch_size, block_m, seqlen_max, n_rows,
+      fdllm::plan_capacity(n_rows, batch_size), static_cast<int32_t*>(plan), fdllm::status_ptr());
+  return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
+}
+
+size_t fdllm_attn_workspace_bytes(int32_t max_items, int32_t n_heads, int32_t kv_splits) {
+  return fdllm::attn_ws_bytes(max_items, n_heads, kv_splits);
+}
+
+int fdllm_attn_cache(const void* q, void* o, const void* k_cache, const void* v_cache, const void* plan,
+                     int32_t max_items, float* attn_scores, float score_scale, int32_t d_model, int32_t n_heads,
+                     int32_t seqlen_max, int64_t n_slots, float softmax_scale, int32_t kv_splits, void* workspace,
+                     size_t workspace_bytes, cudaStream_t stream) {
+  using namespace fdllm;
+  if (n_heads <= 0 || d_model != n_heads * kHD || seqlen_max <= 0 || n_slots <= 0 || max_items < 0 ||
+      kv_splits < 1 || kv_splits > 64)
+    return FDLLM_ERR_ARG;
+  if (max_items == 0) return FDLLM_OK;
+  const void* ptrs[] = {q, o, k_cache, v_cache, plan};
+  for (const void* x : ptrs)
+    if (x == nullptr || !aligned16(x)) return FDLLM_ERR_ARG;
+  CUtensorMap mk, mv;
+  int rc;
+  if ((rc = make_tmap_bf16_sw128(&mk, k_cache, n_slots, d_model, d_model, kKeyTile)) != FDLLM_OK) return rc;
+  if ((rc = make_tmap_bf16_sw128(&mv, v_cache, n_slots, d_model, d_model, kKeyTile)) != FDLLM_OK) return rc;
+  AttnParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.o = static_cast<__nv_bfloat16*>(o);
+  p.kc = static_cast<const __nv_bfloat16*>(k_cache);
+  p.vc = static_cast<const __nv_bfloat16*>(v_cache);
+  p.plan = static_cast<const int32_t*>(plan);
+  p.scores = attn_scores;
+  p.status = status_ptr();
+  p.n_slots = n_slots;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.score_scale = score_scale;
+  p.d_model = d_model;
+  p.n_heads = n_heads;
+  p.seqlen_max = seqlen_max;
+  p.kv_splits = kv_splits;
+  return launch_attn<false>(mk, mv, p, max_items, workspace, workspace_bytes, stream);
+}
+
+int fdllm_verify_attn(const void* q1, const void* k1, const void* v1, void* o, const void* k_cache,
+                      const void* v_cache, const int64_t* pos_k, int64_t n_pos_k, const uint8_t* attn_mask,
+                      const int32_t* verify_blocks, int32_t n_blocks, int32_t block_rows, int32_t n_rows,
+                      int32_t d_model, int32_t n_heads, int64_t n_slots, float softmax_scale, int32_t kv_splits,
+                      void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  using namespace fdllm;
+  if (n_rows <= 0 || n_heads <= 0 || d_model != n_heads * kHD || n_blocks < 0 || block_rows <= 0 || block_rows > 1024 ||
+      n_slots <= 0 || n_pos_k < 0 || kv_splits < 1 || kv_splits > 64)
+    return FDLLM_ERR_ARG;
+  if (n_blocks == 0) return FDLLM_OK;
+  const void* ptrs[] = {q1, k1, v1, o, k_cache, v_cache, attn_mask, verify_blocks};
+  for (const void* x : ptrs)
+    if (x == nullptr) return FDLLM_ERR_ARG;
+  if (!aligned16(q1) || !aligned16(k1) || !aligned16(v1) || !aligned16(k_cache) || !aligned16(v_cache))
+    return FDLLM_ERR_ARG;
+  if (n_pos_k > 0 && pos_k == nullptr) return FDLLM_ERR_ARG;
+  AttnParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q1);
+  p.k1 = static_cast<const __nv_bfloat16*>(k1);
+  p.v1 = static_cast<const __nv_bfloat16*>(v1);
+  p.o = static_cast<__nv_bfloat16*>(o);
+  p.kc = static_cast<const __nv_bfloat16*>(k_cache);
+  p.vc = static_cast<const __nv_bfloat16*>(v_cache);
+  p.pos_k = pos_k;
+  p.n_pos_k = n_pos_k;
+  p.mask = attn_mask;
+  p.vblocks = verify_blocks;
+  p.status = status_ptr();
+  p.n_slots = n_slots;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.d_model = d_model;
+  p.n_heads = n_heads;
+  p.kv_splits = kv_splits;
+  p.n_rows = n_rows;
+  p.block_rows = block_rows;
+  p.row_chunks = (block_rows + kItemRows - 1) / kItemRows;
+  p.n_items = n_blocks * p.row_chunks;
+  CUtensorMap dummy;
+  std::memset(&dummy, 0, sizeof(dummy));
+  return launch_attn<true>(dummy, dummy, p, p.n_items, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,177 @@
+"""Torch-facing wrappers of the C ABI (one function per entry point).
+
+Each wrapper checks dtypes/shapes/devices, passes raw pointers and the
+current CUDA stream to ``libflashdllm_b200.so`` and raises on a non-zero
+status.  Workspaces come from :class:`Workspace`, a per-device buffer that
+grows on demand and is zero-filled when (re)allocated (the kernels leave
+their counters at zero after every call).
+"""
+from __future__ import annotations
+
+import functools
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import call, ptr
+
+BF16 = torch.bfloat16
+
+
+class Workspace:
+    """Grow-only zero-initialised device scratch, one per (device, tag)."""
+
+    _bufs: Dict[Tuple[int, str], torch.Tensor] = {}
+
+    @classmethod
+    def get(cls, device: torch.device, nbytes: int, tag: str = "main") -> torch.Tensor:
+        key = (device.index if device.index is not None else torch.cuda.current_device(), tag)
+        buf = cls._bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            size = max(nbytes, 1 << 20)
+            if buf is not None:
+                size = max(size, int(buf.numel() * 1.5))
+            buf = torch.zeros(size, dtype=torch.uint8, device=device)
+            cls._bufs[key] = buf
+        return buf
+
+    @classmethod
+    def clear(cls) -> None:
+        cls._bufs.clear()
+
+
+def _check(t: torch.Tensor, name: str, dtype=None, dim=None) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (no CPU path)")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if dim is not None and t.dim() != dim:
+        raise ValueError(f"{name} must be {dim}-D, got shape {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+@functools.lru_cache(maxsize=None)
+def _sm_count(index: int) -> int:
+    return torch.cuda.get_device_properties(index).multi_processor_count
+
+
+def auto_kv_splits(items: int, n_heads: int, max_keys: int, device: torch.device) -> int:
+    """Split each key range so the grid covers about two CTAs per SM, keeping
+    at least 128 keys per split."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    target = 2 * _sm_count(idx)
+    s = max(1, -(-target // max(1, items * n_heads)))
+    s = min(s, max(1, max_keys // 128), 16)
+    return s
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _check(x, "x", BF16, 2)
+    _check(weight, "weight", BF16, 1)
+    y = torch.empty_like(x) if out is None else out
+    call("fdllm_rmsnorm", ptr(x), ptr(weight), ptr(y), x.shape[0], x.shape[1], float(eps), _stream())
+    return y
+
+
+def _qkv(entry: str, xn, wq, wk, wv, pos, sin, cos, q_out, k_out, v_out, n_heads: int) -> None:
+    for t, n in ((xn, "xn"), (wq, "wq"), (wk, "wk"), (wv, "wv"), (q_out, "q_out"), (k_out, "k_out"),
+                 (v_out, "v_out")):
+        _check(t, n, BF16, 2)
+    _check(pos, "pos", torch.int64, 1)
+    _check(sin, "rope_sin", torch.float32, 2)
+    _check(cos, "rope_cos", torch.float32, 2)
+    n_rows, d_model = xn.shape
+    if pos.shape[0] < n_rows:
+        raise ValueError("pos shorter than the query rows")
+    # slots index the RoPE tables, and the cache rows when K/V are scattered
+    n_slots = sin.shape[0] if entry == "fdllm_verify_qkv" else min(sin.shape[0], k_out.shape[0])
+    nbytes = _lib.lib().fdllm_qkv_workspace_bytes(n_rows, d_model, n_heads)
+    ws = Workspace.get(xn.device, nbytes, "qkv")
+    call(entry, ptr(xn), ptr(wq), ptr(wk), ptr(wv), ptr(pos), ptr(sin), ptr(cos), ptr(q_out), ptr(k_out),
+         ptr(v_out), n_rows, d_model, n_heads, n_slots, ptr(ws), ws.numel(), _stream())
+
+
+def qkv_rope_cache(xn, wq, wk, wv, pos, sin, cos, q_out, k_cache, v_cache, n_heads: int) -> None:
+    """Q -> ``q_out`` rows, RoPE'd K and V -> ``k_cache/v_cache[pos[r]]``."""
+    _qkv("fdllm_qkv_rope_cache", xn, wq, wk, wv, pos, sin, cos, q_out, k_cache, v_cache, n_heads)
+
+
+def verify_qkv(xn, wq, wk, wv, pos, sin, cos, q_out, k_out, v_out, n_heads: int) -> None:
+    """Q, K, V of the verify rows, all row-indexed (no cache write)."""
+    _qkv("fdllm_verify_qkv", xn, wq, wk, wv, pos, sin, cos, q_out, k_out, v_out, n_heads)
+
+
+def _table(t: Optional[torch.Tensor], dtype) -> Tuple[Optional[torch.Tensor], int]:
+    if t is None or t.numel() == 0:
+        return None, 0
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    t = t.contiguous()
+    if t.dim() != 2 or t.shape[1] != 4:
+        raise ValueError(f"block table must be (n, 4), got {tuple(t.shape)}")
+    return t, t.shape[0]
+
+
+def plan_cache_attention(masked_blocks, tracked_blocks, n_rows: int, batch_size: int, block_m: int,
+                         seqlen_max: int, device: torch.device) -> Tuple[torch.Tensor, int]:
+    """Device work list for :func:`attn_cache`; returns (plan, capacity)."""
+    mb, nm = _table(masked_blocks, torch.int64)
+    tb, nt = _table(tracked_blocks, torch.int64)
+    cap = _lib.lib().fdllm_attn_plan_capacity(n_rows, batch_size)
+    nbytes = _lib.lib().fdllm_attn_plan_bytes(n_rows, batch_size)
+    plan = torch.empty(nbytes // 4, dtype=torch.int32, device=device)
+    call("fdllm_plan_cache_attention", ptr(mb), nm, ptr(tb), nt, n_rows, batch_size, block_m, seqlen_max,
+         ptr(plan), nbytes, _stream())
+    return plan, cap
+
+
+def attn_cache(q, o, k_cache, v_cache, plan: torch.Tensor, capacity: int, attn_scores, score_scale: float,
+               n_heads: int, seqlen_max: int, softmax_scale: float, kv_splits: int = 0) -> None:
+    """Masked + tracked attention over the cache, optional fused score accumulation."""
+    for t, n in ((q, "q"), (o, "o"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _check(t, n, BF16, 2)
+    if attn_scores is not None:
+        _check(attn_scores, "attn_scores", torch.float32)
+    d_model = q.shape[1]
+    if kv_splits <= 0:
+        kv_splits = auto_kv_splits(capacity, n_heads, seqlen_max, q.device)
+    nbytes = _lib.lib().fdllm_attn_workspace_bytes(capacity, n_heads, kv_splits)
+    ws = Workspace.get(q.device, nbytes, "attn")
+    call("fdllm_attn_cache", ptr(q), ptr(o), ptr(k_cache), ptr(v_cache), ptr(plan), capacity, ptr(attn_scores),
+         float(score_scale), d_model, n_heads, seqlen_max, k_cache.shape[0], float(softmax_scale), kv_splits,
+         ptr(ws), ws.numel(), _stream())
+
+
+def verify_attn(q1, k1, v1, o, k_cache, v_cache, pos_k, attn_mask, verify_blocks, block_rows: int, n_heads: int,
+                softmax_scale: float, kv_splits: int = 0, max_keys: Optional[int] = None) -> None:
+    """Flash-Verify attention (gathered cache keys + masked in-block keys)."""
+    for t, n in ((q1, "q1"), (k1, "k1"), (v1, "v1"), (o, "o"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _check(t, n, BF16, 2)
+    vb, nb = _table(verify_blocks, torch.int32)
+    if nb == 0:
+        return
+    if pos_k is not None and pos_k.numel() > 0:
+        pos_k = pos_k.to(torch.int64).contiguous()
+        n_pos = pos_k.numel()
+    else:
+        pos_k, n_pos = None, 0
+    mask = attn_mask.contiguous()
+    if mask.dtype not in (torch.bool, torch.uint8):
+        mask = mask.to(torch.bool)
+    if mask.shape[0] < nb * block_rows or mask.shape[1] != block_rows:
+        raise ValueError(f"attn_mask must be ({nb}*{block_rows}, {block_rows}), got {tuple(mask.shape)}")
+    d_model = q1.shape[1]
+    items = nb * ((block_rows + 63) // 64)
+    if kv_splits <= 0:
+        kv_splits = auto_kv_splits(items, n_heads, max_keys if max_keys is not None else n_pos // nb, q1.device)
+    nbytes = _lib.lib().fdllm_attn_workspace_bytes(items, n_heads, kv_splits)
+    ws = Workspace.get(q1.device, nbytes, "attn")
+    call("fdllm_verify_attn", ptr(q1), ptr(k1), ptr(v1), ptr(o), ptr(k_cache), ptr(v_cache), ptr(pos_k), n_pos,
+         ptr(mask), ptr(vb), nb, block_rows, q1.shape[0], d_model, n_heads, k_cache.shape[0], float(softmax_scale),
+         kv_splits, ptr(ws), ws.numel(), _stream())

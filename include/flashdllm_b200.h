@@ -1,0 +1,137 @@
+/*
+ * flashdllm_b200.h -- C ABI of the B200 (sm_100a) Flash-Cache / Flash-Verify
+ * hot path for LLaDA-style masked-diffusion decoding.
+ *
+ * Every entry point takes raw device pointers, plain integer sizes and a
+ * cudaStream_t, launches asynchronously on that stream and returns an
+ * fdllm status code (0 = success).  Host-side argument checks return
+ * FDLLM_ERR_ARG before anything is launched.  Device-side problems (a cache
+ * slot or key index out of range, a malformed block table, a bounded wait
+ * that ran out) skip the offending access and are recorded in a per-process
+ * device status word that fdllm_status_read() returns and clears.
+ *
+ * Tensors are row-major and contiguous unless a leading dimension is given.
+ * "bf16" means __nv_bfloat16 / torch.bfloat16.  The library allocates no
+ * device memory: callers pass workspaces sized by the *_workspace_bytes()
+ * queries (zero-filled once before first use; the kernels leave them ready
+ * for the next call).
+ *
+ * Citations "ref file:line" name the reference interface each entry point
+ * replaces (VILA-Lab/Flash-dLLM).
+ */
+#ifndef FLASHDLLM_B200_H
+#define FLASHDLLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FDLLM_OK 0
+#define FDLLM_ERR_ARG 1       /* invalid size, pointer or unsupported shape (host check) */
+#define FDLLM_ERR_CUDA 2      /* a CUDA runtime call or kernel launch failed */
+#define FDLLM_ERR_INDEX 3     /* device: cache slot / key / row index out of range */
+#define FDLLM_ERR_TIMEOUT 4   /* device: a bounded wait ran out */
+#define FDLLM_ERR_TABLE 5     /* device: malformed block table */
+#define FDLLM_ERR_WORKSPACE 6 /* workspace too small */
+#define FDLLM_ERR_DRIVER 7    /* TMA descriptor encode unavailable or failed */
+
+/* Library version string. */
+const char* fdllm_version(void);
+
+/* Human-readable name of a status code. */
+const char* fdllm_error_string(int code);
+
+/* Synchronise `stream`, copy the device status word of the current device
+ * into out[0..3] = {first error code, info, kernel id, 0} and clear it.
+ * No reference counterpart (the reference has no error reporting). */
+int fdllm_status_read(int32_t out[4], cudaStream_t stream);
+
+/* RMSNorm as the reference's RMSLayerNorm: y = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))),
+ * x/w/y bf16, rows x dim.  ref llada/model/modeling_llada.py:389-403 (called as
+ * self.attn_norm(x) at llada/flash_cache_triton.py:494). */
+int fdllm_rmsnorm(const void* x, const void* weight, void* y, int32_t rows, int32_t dim, float eps,
+                  cudaStream_t stream);
+
+/* Workspace (bytes) fdllm_qkv_rope_cache / fdllm_verify_qkv need for n_rows query rows. */
+size_t fdllm_qkv_workspace_bytes(int32_t n_rows, int32_t d_model, int32_t n_heads);
+
+/* Fused QKV projection + RoPE + KV-cache scatter (tcgen05/TMEM GEMM fed by TMA).
+ *   xn        bf16 [n_rows, d_model]   RMS-normed hidden states of the query rows
+ *   wq,wk,wv  bf16 [d_model, d_model]  nn.Linear weights (out, in), no bias
+ *   pos       int64 [n_rows]           flat cache slot of each query row
+ *   rope_sin, rope_cos  fp32 [n_slots, head_dim]  tables indexed by flat slot
+ *   q_out     bf16 [n_rows, d_model]   RoPE'd Q, row-indexed
+ *   k_cache, v_cache  bf16 [n_slots, d_model]  RoPE'd K and plain V are written to row pos[r]
+ * head_dim = d_model / n_heads must be 128.  Rows [0, n_rows) are processed:
+ * the caller passes the row span its block table covers.
+ * ref llada/flash_cache_triton.py:15-100 (_flash_qkv_proj_cache_fwd) and its launch at :541-559. */
+int fdllm_qkv_rope_cache(const void* xn, const void* wq, const void* wk, const void* wv, const int64_t* pos,
+                         const float* rope_sin, const float* rope_cos, void* q_out, void* k_cache, void* v_cache,
+                         int32_t n_rows, int32_t d_model, int32_t n_heads, int64_t n_slots, void* workspace,
+                         size_t workspace_bytes, cudaStream_t stream);
+
+/* Verify-query projection: same math as fdllm_qkv_rope_cache, but Q, K and V are all written
+ * row-indexed to q_out/k_out/v_out (bf16 [n_rows, d_model]); the cache is not touched.
+ * ref llada/flash_cache_triton.py:255-338 (_flash_verify_qkv_proj_fwd) and its launch at :505-519. */
+int fdllm_verify_qkv(const void* xn, const void* wq, const void* wk, const void* wv, const int64_t* pos,
+                     const float* rope_sin, const float* rope_cos, void* q_out, void* k_out, void* v_out,
+                     int32_t n_rows, int32_t d_model, int32_t n_heads, int64_t n_slots, void* workspace,
+                     size_t workspace_bytes, cudaStream_t stream);
+
+/* Work-item capacity of an attention plan for n_rows query rows of batch_size sequences
+ * (ceil(n_rows/64) + batch_size), and its size in bytes. */
+int fdllm_attn_plan_capacity(int32_t n_rows, int32_t batch_size);
+size_t fdllm_attn_plan_bytes(int32_t n_rows, int32_t batch_size);
+
+/* Build the attention work list from the reference's block tables (device int64 [n, 4] rows
+ * (seq, k_end, q_start, q_end); masked tiles first in the row space, then tracked tiles).
+ * Each work item is up to 64 query rows of one sequence (its masked rows first), so one pass
+ * over the sequence's K/V serves masked and tracked rows together.  Malformed tables
+ * (k_end outside (0, seqlen_max], a tile taller than block_m, more than one masked tile per
+ * sequence, tracked tiles of a sequence not contiguous, tiles of one sequence with different
+ * k_end) are reported as FDLLM_ERR_TABLE and yield an empty plan.
+ * ref llada/generate.py:52-58,146-163,439-465 (make_blocks / block tables) as consumed by
+ * llada/flash_cache_triton.py:561-607. */
+int fdllm_plan_cache_attention(const int64_t* masked_blocks, int32_t n_masked, const int64_t* tracked_blocks,
+                               int32_t n_tracked, int32_t n_rows, int32_t batch_size, int32_t block_m,
+                               int32_t seqlen_max, void* plan, size_t plan_bytes, cudaStream_t stream);
+
+/* Workspace (bytes) for fdllm_attn_cache / fdllm_verify_attn with the given item count and split count. */
+size_t fdllm_attn_workspace_bytes(int32_t max_items, int32_t n_heads, int32_t kv_splits);
+
+/* Block-table scheduled attention over the KV cache for masked + tracked rows.
+ *   q          bf16 [n_rows, d_model];  o  bf16 [n_rows, d_model]
+ *   k_cache, v_cache  bf16 [n_slots, d_model]; sequence b owns slots [b*seqlen_max, b*seqlen_max+k_end)
+ *   plan       from fdllm_plan_cache_attention; max_items = fdllm_attn_plan_capacity(...)
+ *   attn_scores  fp32 [batch*seqlen_max] or NULL: when given, for every key n of sequence b
+ *              attn_scores[b*seqlen_max + n] += score_scale * sum over masked rows and heads of the
+ *              raw (unscaled) q.k logit -- the reference's S tensor + S.mean((0,1)) fused.
+ *   kv_splits  split of each sequence's key range over CTAs (1 = none; partials combined on device)
+ * ref llada/flash_cache_triton.py:103-252 (_flash_masked_attention_fwd, _flash_tracked_attention_fwd)
+ * and :538, :614-615 (S and attn_scores). */
+int fdllm_attn_cache(const void* q, void* o, const void* k_cache, const void* v_cache, const void* plan,
+                     int32_t max_items, float* attn_scores, float score_scale, int32_t d_model, int32_t n_heads,
+                     int32_t seqlen_max, int64_t n_slots, float softmax_scale, int32_t kv_splits, void* workspace,
+                     size_t workspace_bytes, cudaStream_t stream);
+
+/* Flash-Verify attention: rows [q_s, q_e) of verify block row b = (k_s, k_e, q_s, q_e) (int32
+ * [n_blocks, 4]) attend to cache rows pos_k[k_s:k_e] (gathered) and to their own block's fresh
+ * k1/v1 rows under attn_mask (bool/uint8 [n_blocks*block_rows, block_rows]); block_rows = 2*block_m.
+ * The in-block part is merged with a re-stabilised online softmax (the reference reuses the
+ * cache part's running max, which yields NaN rows when a sequence has no cache keys).
+ * ref llada/flash_cache_triton.py:341-428 (_flash_verify_attention_fwd) and its launch at :521-535. */
+int fdllm_verify_attn(const void* q1, const void* k1, const void* v1, void* o, const void* k_cache,
+                      const void* v_cache, const int64_t* pos_k, int64_t n_pos_k, const uint8_t* attn_mask,
+                      const int32_t* verify_blocks, int32_t n_blocks, int32_t block_rows, int32_t n_rows,
+                      int32_t d_model, int32_t n_heads, int64_t n_slots, float softmax_scale, int32_t kv_splits,
+                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHDLLM_B200_H */

@@ -1,0 +1,191 @@
+"""GPU parity of the block-table attention (Flash-Cache, fused masked +
+tracked rows with the attention-score accumulation) and of the Flash-Verify
+attention against the CPU oracle (the reference kernels' semantics, bf16
+inputs, P rounded to bf16 like the reference).  Outputs: max |cuda - oracle| /
+max |oracle| <= 2e-2; accumulated scores: <= 1e-3 (fp32 sums of the same
+bf16 products in a different order)."""
+import numpy as np
+import pytest
+import torch
+
+import cases
+from oracle import decode_oracle as do
+from oracle import flash_cache_oracle as fco
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+SCORE_TOL = 1e-3
+
+
+def _rel(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-6)).item()
+
+
+def _tiles(j, k_end, start, n, bm):
+    return [(j, k_end, s, min(s + bm, start + n)) for s in range(start, start + n, bm)]
+
+
+def _cache_inputs(k_ends, masked, tracked, d_model, lmax, bm, seed):
+    g = torch.Generator().manual_seed(seed)
+    B = len(k_ends)
+    rows_m, rows_t, acc = [], [], 0
+    for j in range(B):
+        if masked[j]:
+            rows_m += _tiles(j, k_ends[j], acc, masked[j], bm)
+            acc += masked[j]
+    for j in range(B):
+        if tracked[j]:
+            rows_t += _tiles(j, k_ends[j], acc, tracked[j], bm)
+            acc += tracked[j]
+    n_rows = acc
+    q = torch.randn(n_rows, d_model, generator=g).bfloat16()
+    kc = torch.randn(B * lmax, d_model, generator=g).bfloat16()
+    vc = torch.randn(B * lmax, d_model, generator=g).bfloat16()
+    mb = torch.tensor(rows_m, dtype=torch.int64).reshape(-1, 4)
+    tb = torch.tensor(rows_t, dtype=torch.int64).reshape(-1, 4)
+    return q, kc, vc, mb, tb, n_rows
+
+
+def _run_cache(q, kc, vc, mb, tb, n_rows, lmax, bm, n_heads, B, kv_splits=0, scores=True):
+    import flash_dllm_b200.ops as ops
+    from flash_dllm_b200._lib import check_device_status
+    dev = torch.device("cuda")
+    scale = 1.0 / 128 ** 0.5
+    qd, kd, vd = q.to(dev), kc.to(dev), vc.to(dev)
+    o = torch.zeros_like(qd)
+    sc = torch.zeros(B * lmax, dtype=torch.float32, device=dev) if scores else None
+    plan, cap = ops.plan_cache_attention(mb.to(dev), tb.to(dev), n_rows, B, bm, lmax, dev)
+    ops.attn_cache(qd, o, kd, vd, plan, cap, sc, 1.0 / (bm * n_heads), n_heads, lmax, scale, kv_splits)
+    check_device_status()
+    return o, sc
+
+
+def _oracle_cache(q, kc, vc, mb, tb, lmax, bm, n_heads, B):
+    scale = 1.0 / 128 ** 0.5
+    o = torch.zeros(q.shape)
+    S = torch.zeros((bm, n_heads, B, lmax))
+    if mb.shape[0]:
+        fco.cache_attention(q, o, kc, vc, mb, lmax, n_heads, bm, scale, 128, S)
+    if tb.shape[0]:
+        fco.cache_attention(q, o, kc, vc, tb, lmax, n_heads, bm, scale, 128, None)
+    return o, S.mean((0, 1)).view(-1)
+
+
+def test_cache_attention_golden_case():
+    c = cases.cache_case()
+    q = c["xn"].bfloat16()
+    kc, vc = c["k_cache"].bfloat16(), c["v_cache"].bfloat16()
+    o, sc = _run_cache(q, kc, vc, c["masked_blocks"], c["tracked_blocks"], q.shape[0], cases.LMAX,
+                       cases.BLOCK_M, cases.N_HEADS, 2)
+    oo, so = _oracle_cache(q, kc, vc, c["masked_blocks"], c["tracked_blocks"], cases.LMAX, cases.BLOCK_M,
+                           cases.N_HEADS, 2)
+    assert _rel(o, oo) <= TOL
+    assert _rel(sc, so) <= SCORE_TOL
+
+
+@pytest.mark.parametrize("kv_splits", [0, 1, 3])
+def test_cache_attention_config2_shape(kv_splits):
+    """BASELINE config 2 shape: 8 sequences, k_end uniform in [256,1024] step
+    32, 32 masked rows + 0..32 refresh rows each, 32 heads x 128."""
+    rs = np.random.RandomState(5)
+    B, bm, lmax, H = 8, 32, 1024, 32
+    k_ends = [int(x) for x in rs.choice(np.arange(256, 1025, 32), B)]
+    tracked = [int(x) for x in rs.randint(0, 33, B)]
+    tracked[2] = 0
+    q, kc, vc, mb, tb, n = _cache_inputs(k_ends, [bm] * B, tracked, H * 128, lmax, bm, seed=11)
+    o, sc = _run_cache(q, kc, vc, mb, tb, n, lmax, bm, H, B, kv_splits)
+    oo, so = _oracle_cache(q, kc, vc, mb, tb, lmax, bm, H, B)
+    assert _rel(o, oo) <= TOL
+    assert _rel(sc, so) <= SCORE_TOL
+
+
+def test_cache_attention_prefill_rows_and_no_scores():
+    """Hundreds of tracked rows per sequence (the first decode step) -> several
+    work items per sequence; the score output may be omitted."""
+    B, bm, lmax, H = 2, 32, 768, 4
+    q, kc, vc, mb, tb, n = _cache_inputs([768, 640], [bm, bm], [600, 300], H * 128, lmax, bm, seed=3)
+    o, _ = _run_cache(q, kc, vc, mb, tb, n, lmax, bm, H, B, scores=False)
+    oo, _ = _oracle_cache(q, kc, vc, mb, tb, lmax, bm, H, B)
+    assert _rel(o, oo) <= TOL
+
+
+def test_cache_attention_block128_masked_spans_items():
+    B, bm, lmax, H = 2, 128, 512, 2
+    q, kc, vc, mb, tb, n = _cache_inputs([384, 512], [bm, 100], [200, 17], H * 128, lmax, bm, seed=4)
+    o, sc = _run_cache(q, kc, vc, mb, tb, n, lmax, bm, H, B)
+    oo, so = _oracle_cache(q, kc, vc, mb, tb, lmax, bm, H, B)
+    assert _rel(o, oo) <= TOL
+    assert _rel(sc, so) <= SCORE_TOL
+
+
+def test_malformed_table_is_reported():
+    import flash_dllm_b200.ops as ops
+    from flash_dllm_b200._lib import FdllmError, check_device_status
+    dev = torch.device("cuda")
+    mb = torch.tensor([[0, 999, 0, 16]], dtype=torch.int64, device=dev)  # k_end > seqlen_max
+    plan, cap = ops.plan_cache_attention(mb, None, 16, 1, 16, 256, dev)
+    with pytest.raises(FdllmError):
+        check_device_status()
+    assert int(plan[0]) == 0  # empty plan: the attention kernel does nothing
+
+
+def _verify_inputs(s_list, n_keys, d_model, lmax, bm, seed):
+    rs = np.random.RandomState(seed)
+    g = torch.Generator().manual_seed(seed)
+    bm2 = 2 * bm
+    q_pos, k_pos, rows, masks = [], [], [], []
+    acc_q = acc_k = 0
+    for j, (s, nk) in enumerate(zip(s_list, n_keys)):
+        perm = rs.permutation(lmax) + j * lmax
+        t = bm2 - 2 * s
+        q_pos.append(np.concatenate([perm[:t], perm[t:t + s], perm[t:t + s]]))
+        k_pos.append(perm[t + s: t + s + nk])
+        rows.append((acc_k, acc_k + nk, acc_q, acc_q + bm2))
+        masks.append(do.verify_mask(bm, s))
+        acc_q += bm2
+        acc_k += nk
+    B = len(s_list)
+    n = acc_q
+    return dict(
+        q1=torch.randn(n, d_model, generator=g).bfloat16(), k1=torch.randn(n, d_model, generator=g).bfloat16(),
+        v1=torch.randn(n, d_model, generator=g).bfloat16(),
+        kc=torch.randn(B * lmax, d_model, generator=g).bfloat16(),
+        vc=torch.randn(B * lmax, d_model, generator=g).bfloat16(),
+        pos_k=torch.from_numpy(np.concatenate(k_pos).astype(np.int64)),
+        blocks=torch.tensor(rows, dtype=torch.int32), mask=torch.cat(masks, 0))
+
+
+def _check_verify(v, bm, H, kv_splits=0):
+    import flash_dllm_b200.ops as ops
+    from flash_dllm_b200._lib import check_device_status
+    dev = torch.device("cuda")
+    scale = 1.0 / 128 ** 0.5
+    d = {k: t.to(dev) for k, t in v.items()}
+    o = torch.zeros_like(d["q1"])
+    ops.verify_attn(d["q1"], d["k1"], d["v1"], o, d["kc"], d["vc"], d["pos_k"], d["mask"], d["blocks"], 2 * bm, H,
+                    scale, kv_splits)
+    check_device_status()
+    oo = torch.zeros(v["q1"].shape)
+    fco.verify_attention(v["q1"], v["k1"], v["v1"], oo, v["kc"], v["vc"], v["pos_k"], v["mask"], v["blocks"], H,
+                         2 * bm, scale, 64)
+    assert _rel(o, oo) <= TOL
+
+
+def test_verify_attention_golden_case():
+    c = cases.verify_case()
+    v = dict(q1=c["xn"].bfloat16(), k1=(c["xn"] * 0.5).bfloat16(), v1=(c["xn"] * -0.7).bfloat16(),
+             kc=c["k_cache"].bfloat16(), vc=c["v_cache"].bfloat16(), pos_k=c["pos_k"], blocks=c["blocks"],
+             mask=c["attn_mask"])
+    _check_verify(v, cases.BLOCK_M, cases.N_HEADS)
+
+
+@pytest.mark.parametrize("kv_splits", [0, 1, 4])
+def test_verify_attention_config4_shape(kv_splits):
+    """bm 32 -> 64 verify rows per sequence, 8 sequences, 32 heads, ~830
+    gathered cache keys each, varied draft counts S (0..16)."""
+    rs = np.random.RandomState(9)
+    s_list = [0, 16, 3, 8, 1, 16, 12, 5]
+    n_keys = [int(896 - 64 + s + rs.randint(-20, 1)) - s for s in s_list]
+    v = _verify_inputs(s_list, n_keys, 32 * 128, 896, 32, seed=21)
+    _check_verify(v, 32, 32, kv_splits)
