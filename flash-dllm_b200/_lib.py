@@ -39,6 +39,11 @@ SIGNATURES = {
                                 _p]),
     "fdllm_verify_attn": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32, _i64,
                                  _f32, _i32, _p, _sz, _p]),
+    "fdllm_row_stats": (_int, [_p, _i64, _i32, _i32, _p, _p, _p, _p, _p]),
+    "fdllm_window_accept": (_int, [_p, _p, _p, _p, _p, _i32, _i64, _i64, _f64, _i32, _i64, _p, _p, _p, _p, _p, _p,
+                                   _p]),
+    "fdllm_verify_accept": (_int, [_p, _p, _p, _p, _p, _i32, _i64, _f64, _i64, _p, _p, _p, _p]),
+    "fdllm_refresh_sort": (_int, [_p, _i32, _i64, _p, _p, _i64, _p]),
 }
 
 

@@ -1,0 +1,389 @@
+// Decode bookkeeping kernels of the Flash-Cache / Flash-Verify loop
+// (llada/generate.py), batched over sequences so one step needs one launch
+// per decision instead of per-sequence host loops:
+//
+//   row_stats      fp64 softmax statistics of logit rows: max probability,
+//                  first argmax, and optionally the probability of a given
+//                  token (one CTA per row, two passes over the vocabulary).
+//   window_accept  per sequence (one warp): zero probabilities past the
+//                  predicted length, stable descending order of the masked
+//                  window, keep = max(#(p >= threshold), min_keep), write the
+//                  reordered window into full_pos, commit the kept tokens,
+//                  record drafts and the EOS position.
+//   verify_accept  per sequence: sequential fp64 cumprod of the drafts'
+//                  mask-view probabilities, keep = #(cumprod >= gamma),
+//                  commit the accepted drafts.
+//   refresh_sort   per sequence (one CTA): stable ascending sort of the
+//                  decoded slots by attention score, in place in full_pos
+//                  (bitonic sort of unique (score, index) keys in smem).
+//
+// Integer outputs equal the reference's decisions whenever its torch.sort
+// calls resolve ties in index order (the reference's sorts are not stable).
+#include "common.cuh"
+#include "internal.h"
+
+namespace fdllm {
+
+constexpr int kStatsThreads = 512;
+constexpr int kDecodeKernelId = 5;
+constexpr int kRefreshMax = 8192;
+
+__device__ __forceinline__ float bf16_to_f(__nv_bfloat16 h) { return __bfloat162float(h); }
+
+// ------------------------------------------------------------ row stats ----
+__global__ void __launch_bounds__(kStatsThreads) row_stats_kernel(const __nv_bfloat16* __restrict__ logits,
+                                                                  int64_t ld, int vocab,
+                                                                  const int64_t* __restrict__ tokens,
+                                                                  double* __restrict__ p_max,
+                                                                  int64_t* __restrict__ argmax,
+                                                                  double* __restrict__ p_tok) {
+  const int64_t r = blockIdx.x;
+  const __nv_bfloat16* row = logits + r * ld;
+  __shared__ float s_max[kStatsThreads / 32];
+  __shared__ int s_idx[kStatsThreads / 32];
+  __shared__ double s_sum[kStatsThreads / 32];
+  float m = -INFINITY;
+  int mi = INT32_MAX;
+  for (int i = threadIdx.x; i < vocab; i += kStatsThreads) {
+    const float v = bf16_to_f(row[i]);
+    if (v > m) {  // strictly greater: first index wins within a thread (indices increase)
+      m = v;
+      mi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, mi, o);
+    if (om > m || (om == m && oi < mi)) {
+      m = om;
+      mi = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    s_max[w] = m;
+    s_idx[w] = mi;
+  }
+  __syncthreads();
+  if (w == 0) {
+    m = l < kStatsThreads / 32 ? s_max[l] : -INFINITY;
+    mi = l < kStatsThreads / 32 ? s_idx[l] : INT32_MAX;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, mi, o);
+      if (om > m || (om == m && oi < mi)) {
+        m = om;
+        mi = oi;
+      }
+    }
+    if (l == 0) {
+      s_max[0] = m;
+      s_idx[0] = mi;
+    }
+  }
+  __syncthreads();
+  const double md = static_cast<double>(s_max[0]);
+  double sum = 0.0;
+  for (int i = threadIdx.x; i < vocab; i += kStatsThreads) sum += exp(static_cast<double>(bf16_to_f(row[i])) - md);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (l == 0) s_sum[w] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int i = 0; i < kStatsThreads / 32; ++i) t += s_sum[i];
+    p_max[r] = 1.0 / t;
+    argmax[r] = s_idx[0];
+    if (p_tok != nullptr) {
+      const int64_t tk = tokens[r];
+      p_tok[r] = (tk >= 0 && tk < vocab) ? exp(static_cast<double>(bf16_to_f(row[tk])) - md) / t : 0.0;
+    }
+  }
+}
+
+// -------------------------------------------------------- window accept ----
+// seq_info int64 [B, 4]: (row offset into p/argmax/window, window length, num_decoded, predicted_length).
+// eos_known int32 [B]: 1 when an EOS was decoded earlier (probabilities past the
+// predicted length are zeroed).  Outputs per sequence: keep, length_num (window
+// slots before the predicted length), eos_slot (largest committed slot holding
+// eos_id, or -1).
+struct AcceptArgs {
+  const double* p;
+  const int64_t* tok;
+  const int64_t* window;   // flat slots of the masked window rows
+  const int64_t* seq_info;
+  const int32_t* eos_known;
+  int64_t* full_pos;       // [B, lmax]
+  int64_t* x;              // [B * lmax]
+  int64_t* x_draft;        // [B * lmax] or null
+  int32_t* keep_out;
+  int32_t* length_out;
+  int64_t* eos_out;
+  int32_t* status;
+  int64_t lmax;
+  int64_t eos_id;
+  double threshold;
+  int32_t min_keep;
+  int32_t batch;        // sequences in this call
+  int64_t batch_slots;  // rows of full_pos; x and x_draft hold batch_slots * lmax tokens
+};
+
+constexpr int kAcceptMax = 256;
+
+__global__ void __launch_bounds__(32) window_accept_kernel(const AcceptArgs a) {
+  const int j = blockIdx.x;
+  const int lane = threadIdx.x;
+  const int64_t off = a.seq_info[4 * j + 0];
+  const int n = static_cast<int>(a.seq_info[4 * j + 1]);
+  const int64_t fp_at = a.seq_info[4 * j + 2];  // flat index of full_pos[slot, num_decoded]
+  const int64_t pred = a.seq_info[4 * j + 3];
+  const int64_t nd = fp_at >= 0 ? fp_at % a.lmax : -1;
+  if (n <= 0 || n > kAcceptMax || nd < 0 || fp_at >= a.lmax * a.batch_slots || nd + n > a.lmax) {
+    if (lane == 0) {
+      if (n != 0) report(a.status, FDLLM_ERR_ARG, j, kDecodeKernelId);
+      a.keep_out[j] = 0;
+      a.length_out[j] = 0;
+      a.eos_out[j] = -1;
+    }
+    return;
+  }
+  __shared__ double sp[kAcceptMax];
+  __shared__ int64_t sslot[kAcceptMax], stok[kAcceptMax];
+  __shared__ int64_t sorted_slot[kAcceptMax], sorted_tok[kAcceptMax];
+  const bool zero_tail = a.eos_known[j] != 0;
+  int above = 0, within = 0;
+  for (int i = lane; i < n; i += 32) {
+    double pv = a.p[off + i];
+    const int64_t slot = a.window[off + i];
+    const bool tail = slot >= pred;
+    if (zero_tail && tail) pv = 0.0;
+    sp[i] = pv;
+    sslot[i] = slot;
+    stok[i] = a.tok[off + i];
+    above += pv >= a.threshold ? 1 : 0;
+    within += (zero_tail && tail) ? 0 : 1;
+    if (a.x_draft != nullptr && slot >= 0 && slot < a.lmax * a.batch_slots) a.x_draft[slot] = stok[i];
+  }
+  __syncwarp();
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    above += __shfl_xor_sync(0xffffffffu, above, o);
+    within += __shfl_xor_sync(0xffffffffu, within, o);
+  }
+  // stable descending rank: #greater + #equal-before
+  for (int i = lane; i < n; i += 32) {
+    const double pi = sp[i];
+    int rank = 0;
+    for (int k = 0; k < n; ++k) {
+      const double pk = sp[k];
+      rank += (pk > pi || (pk == pi && k < i)) ? 1 : 0;
+    }
+    sorted_slot[rank] = sslot[i];
+    sorted_tok[rank] = stok[i];
+  }
+  __syncwarp();
+  const int keep = max(above, a.min_keep) < n ? max(above, a.min_keep) : n;
+  int64_t* fp = a.full_pos + fp_at;
+  int64_t eos = -1;
+  for (int i = lane; i < n; i += 32) {
+    const int64_t slot = sorted_slot[i];
+    fp[i] = slot;
+    if (i < keep && slot >= 0 && slot < a.lmax * a.batch_slots) {
+      a.x[slot] = sorted_tok[i];
+      if (sorted_tok[i] == a.eos_id) eos = max(eos, slot);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const int64_t oe = __shfl_xor_sync(0xffffffffu, eos, o);
+    eos = oe > eos ? oe : eos;
+  }
+  if (lane == 0) {
+    a.keep_out[j] = keep;
+    a.length_out[j] = within;
+    a.eos_out[j] = eos;
+  }
+}
+
+// -------------------------------------------------------- verify accept ----
+// seq_info int64 [B, 4]: (row offset into p/draft tokens, number of drafts S,
+// num_decoded, predicted_length); eos_known as above; draft_slots are the flat
+// slots of the draft rows (full_pos[j, nd:nd+S]).
+struct VerifyArgs {
+  const double* p;
+  const int64_t* draft_tok;
+  const int64_t* draft_slot;
+  const int64_t* seq_info;
+  const int32_t* eos_known;
+  int64_t* x;
+  int32_t* keep_out;
+  int64_t* eos_out;
+  int32_t* status;
+  int64_t n_slots;
+  int64_t eos_id;
+  double gamma;
+  int32_t batch;
+};
+
+__global__ void verify_accept_kernel(const VerifyArgs a) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= a.batch) return;
+  const int64_t off = a.seq_info[4 * j + 0];
+  const int s = static_cast<int>(a.seq_info[4 * j + 1]);
+  const int64_t pred = a.seq_info[4 * j + 3];
+  const bool zero_tail = a.eos_known[j] != 0;
+  double cp = 1.0;
+  int keep = 0;
+  for (int i = 0; i < s; ++i) {  // sequential product: the order of torch.cumprod on the CPU
+    double pv = a.p[off + i];
+    if (zero_tail && a.draft_slot[off + i] >= pred) pv = 0.0;
+    cp *= pv;
+    keep += cp >= a.gamma ? 1 : 0;
+  }
+  int64_t eos = -1;
+  for (int i = 0; i < keep; ++i) {
+    const int64_t slot = a.draft_slot[off + i];
+    if (slot < 0 || slot >= a.n_slots) {
+      report(a.status, FDLLM_ERR_INDEX, j, kDecodeKernelId);
+      continue;
+    }
+    a.x[slot] = a.draft_tok[off + i];
+    if (a.draft_tok[off + i] == a.eos_id) eos = slot > eos ? slot : eos;
+  }
+  a.keep_out[j] = keep;
+  a.eos_out[j] = eos;
+}
+
+// --------------------------------------------------------- refresh sort ----
+// Orderable 32-bit image of a float for ascending order; -0 sorts as +0 and
+// NaN after +inf (torch.sort's placement).
+__device__ __forceinline__ uint32_t float_key(float f) {
+  if (f != f) return 0xFFFFFFFFu;
+  if (f == 0.f) f = 0.f;
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// counts int64 [B]: number of leading full_pos entries of each sequence to sort.
+__global__ void __launch_bounds__(1024) refresh_sort_kernel(int64_t* __restrict__ full_pos, int64_t lmax,
+                                                            const int64_t* __restrict__ counts,
+                                                            const float* __restrict__ scores, int64_t n_slots,
+                                                            int32_t* status) {
+  extern __shared__ uint64_t keys[];
+  const int j = blockIdx.x;
+  const int n = static_cast<int>(counts[j]);
+  if (n <= 1) return;
+  if (n > kRefreshMax || n > lmax) {
+    if (threadIdx.x == 0) report(status, FDLLM_ERR_ARG, j, kDecodeKernelId);
+    return;
+  }
+  int64_t* fp = full_pos + static_cast<int64_t>(j) * lmax;
+  int pow2 = 1;
+  while (pow2 < n) pow2 <<= 1;
+  for (int i = threadIdx.x; i < pow2; i += blockDim.x) {
+    if (i < n) {
+      const int64_t slot = fp[i];
+      const float sc = (slot >= 0 && slot < n_slots) ? scores[slot] : INFINITY;
+      keys[i] = (static_cast<uint64_t>(float_key(sc)) << 32) | static_cast<uint32_t>(i);
+    } else {
+      keys[i] = ~0ull;
+    }
+  }
+  __syncthreads();
+  for (int k = 2; k <= pow2; k <<= 1) {
+    for (int jj = k >> 1; jj > 0; jj >>= 1) {
+      for (int i = threadIdx.x; i < pow2; i += blockDim.x) {
+        const int ixj = i ^ jj;
+        if (ixj > i) {
+          const uint64_t a = keys[i], b = keys[ixj];
+          const bool up = (i & k) == 0;
+          if ((a > b) == up) {
+            keys[i] = b;
+            keys[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // gather: new position i takes the slot that was at index (key & 0xffffffff)
+  int64_t tmp[kRefreshMax / 1024];
+  const int per = (n + blockDim.x - 1) / blockDim.x;  // <= 8 for n <= 8192
+  for (int t = 0; t < per; ++t) {
+    const int i = threadIdx.x + t * blockDim.x;
+    tmp[t] = i < n ? fp[static_cast<uint32_t>(keys[i] & 0xFFFFFFFFull)] : 0;
+  }
+  __syncthreads();
+  for (int t = 0; t < per; ++t) {
+    const int i = threadIdx.x + t * blockDim.x;
+    if (i < n) fp[i] = tmp[t];
+  }
+}
+
+}  // namespace fdllm
+
+extern "C" {
+
+int fdllm_row_stats(const void* logits, int64_t ld, int32_t n_rows, int32_t vocab, const int64_t* tokens,
+                    double* p_max, int64_t* argmax, double* p_tok, cudaStream_t stream) {
+  if (n_rows < 0 || vocab <= 0 || ld < vocab || logits == nullptr || p_max == nullptr || argmax == nullptr ||
+      (p_tok != nullptr && tokens == nullptr))
+    return FDLLM_ERR_ARG;
+  if (n_rows == 0) return FDLLM_OK;
+  fdllm::row_stats_kernel<<<n_rows, fdllm::kStatsThreads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(logits), ld, vocab, tokens, p_max, argmax, p_tok);
+  return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
+}
+
+int fdllm_window_accept(const double* p, const int64_t* tok, const int64_t* window, const int64_t* seq_info,
+                        const int32_t* eos_known, int32_t batch, int64_t batch_slots, int64_t lmax, double threshold,
+                        int32_t min_keep, int64_t eos_id, int64_t* full_pos, int64_t* x, int64_t* x_draft,
+                        int32_t* keep_out, int32_t* length_out, int64_t* eos_out, cudaStream_t stream) {
+  if (batch < 0 || lmax <= 0 || min_keep < 0 || batch_slots <= 0) return FDLLM_ERR_ARG;
+  if (batch == 0) return FDLLM_OK;
+  const void* ptrs[] = {p, tok, window, seq_info, eos_known, full_pos, x, keep_out, length_out, eos_out};
+  for (const void* q : ptrs)
+    if (q == nullptr) return FDLLM_ERR_ARG;
+  fdllm::AcceptArgs a{p, tok, window, seq_info, eos_known, full_pos, x, x_draft, keep_out, length_out, eos_out,
+                      fdllm::status_ptr(), lmax, eos_id, threshold, min_keep, batch, batch_slots};
+  fdllm::window_accept_kernel<<<batch, 32, 0, stream>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
+}
+
+int fdllm_verify_accept(const double* p, const int64_t* draft_tok, const int64_t* draft_slot,
+                        const int64_t* seq_info, const int32_t* eos_known, int32_t batch, int64_t n_slots,
+                        double gamma, int64_t eos_id, int64_t* x, int32_t* keep_out, int64_t* eos_out,
+                        cudaStream_t stream) {
+  if (batch < 0 || n_slots <= 0) return FDLLM_ERR_ARG;
+  if (batch == 0) return FDLLM_OK;
+  const void* ptrs[] = {seq_info, eos_known, x, keep_out, eos_out};
+  for (const void* q : ptrs)
+    if (q == nullptr) return FDLLM_ERR_ARG;
+  fdllm::VerifyArgs a{p, draft_tok, draft_slot, seq_info, eos_known, x, keep_out, eos_out, fdllm::status_ptr(),
+                      n_slots, eos_id, gamma, batch};
+  fdllm::verify_accept_kernel<<<(batch + 127) / 128, 128, 0, stream>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
+}
+
+int fdllm_refresh_sort(int64_t* full_pos, int32_t batch, int64_t lmax, const int64_t* counts, const float* scores,
+                       int64_t n_slots, cudaStream_t stream) {
+  if (batch < 0 || lmax <= 0 || full_pos == nullptr || counts == nullptr || scores == nullptr) return FDLLM_ERR_ARG;
+  if (batch == 0) return FDLLM_OK;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int smem = fdllm::kRefreshMax * sizeof(uint64_t);
+  if (dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(fdllm::refresh_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return FDLLM_ERR_CUDA;
+    attr[dev] = true;
+  }
+  fdllm::refresh_sort_kernel<<<batch, 1024, smem, stream>>>(full_pos, lmax, counts, scores, n_slots,
+                                                             fdllm::status_ptr());
+  return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,110 @@
+"""Drop-in replacement of the reference's fused layer operator.
+
+``flash_fused_elastic_cache(self, x, block_idx, positions, lengths,
+softmax_scale=None)`` has the signature, argument meaning and side effects of
+``llada/flash_cache_triton.py:462-638``: ``self`` is a LLaMA-style LLaDA
+block (``config.d_model/n_heads``, ``attn_norm``, ``q_proj/k_proj/v_proj``,
+``attn_out``, ``ff_norm``, ``ff_proj``, ``up_proj``, ``act``, ``ff_out``,
+``dropout`` and the per-layer ``k_cache``/``v_cache`` set by the decode
+driver); ``positions``/``lengths`` are the driver's lists; the caches and
+``attn_scores`` are updated in place; the return value is the block output
+``(1, Nq, d_model)``.
+
+The attention half runs on this package's sm_100a kernels: RMSNorm, the
+tcgen05 QKV + RoPE + cache-scatter GEMM (or its verify variant), and one
+fused masked + tracked attention pass (or the verify attention).  The
+reference's ``S`` tensor and ``attn_scores += S.mean((0, 1))`` become an
+in-kernel accumulation.  The projections after attention (``attn_out`` and
+the SwiGLU MLP) are the block's own ``nn.Linear`` modules, as in the
+reference.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import ops
+
+
+def _norm(module, x: torch.Tensor) -> torch.Tensor:
+    w = getattr(module, "weight", None)
+    if w is None or w.dtype != torch.bfloat16 or getattr(module, "bias", None) is not None:
+        raise TypeError("flash_fused_elastic_cache needs bf16 RMSNorm modules with a weight and no bias")
+    return ops.rmsnorm(x, w, float(getattr(module, "eps", 1e-5)))
+
+
+class _PlanCache:
+    """The attention plan of one forward pass: every layer of a forward gets
+    the same block-table tensor objects, so the plan is built at the first
+    layer and reused by the others (the tensors are held, so their identity
+    cannot be recycled while cached)."""
+
+    def __init__(self):
+        self.key = None
+        self.value = None
+
+    def get(self, masked, tracked, n_rows, batch, block_m, max_length, device):
+        key = (masked, tracked, n_rows, batch, block_m, max_length, device)
+        if self.key is not None and all(a is b if isinstance(a, torch.Tensor) else a == b
+                                        for a, b in zip(self.key, key)):
+            return self.value
+        self.value = ops.plan_cache_attention(masked, tracked, n_rows, batch, block_m, max_length, device)
+        self.key = key
+        return self.value
+
+
+_PLANS = _PlanCache()
+
+
+def flash_fused_elastic_cache(self, x: torch.Tensor, block_idx, positions, lengths, softmax_scale: float = None):
+    query_pos_flat, key_pos_flat, rotary_emb_pos, _info, attn_scores, attn_mask = positions
+    (_start_layer, query_verify_blocks, query_masked_blocks, query_tracked_blocks, _query_blocks, active_batch,
+     _num_active, max_length, block_m, _block_n, _elastic, verify) = lengths
+    d_model = self.config.d_model
+    n_heads = self.config.n_heads
+    head_dim = d_model // n_heads
+    softmax_scale = softmax_scale or (1.0 / math.sqrt(head_dim))
+    x = x.contiguous()
+    n_rows = x.shape[0]
+    x_normed = _norm(self.attn_norm, x)
+    att = torch.empty_like(x)
+    q = torch.empty_like(x)
+    sin, cos = rotary_emb_pos
+    wq, wk, wv = self.q_proj.weight, self.k_proj.weight, self.v_proj.weight
+
+    if verify:
+        k1 = torch.empty_like(x)
+        v1 = torch.empty_like(x)
+        ops.verify_qkv(x_normed, wq, wk, wv, query_pos_flat, sin, cos, q, k1, v1, n_heads)
+        ops.verify_attn(q, k1, v1, att, self.k_cache, self.v_cache, key_pos_flat, attn_mask, query_verify_blocks,
+                        2 * block_m, n_heads, softmax_scale, max_keys=max_length)
+    else:
+        if n_rows > 0:
+            ops.qkv_rope_cache(x_normed, wq, wk, wv, query_pos_flat, sin, cos, q, self.k_cache, self.v_cache,
+                               n_heads)
+            plan, cap = _PLANS.get(query_masked_blocks, query_tracked_blocks, n_rows, len(active_batch), block_m,
+                                   max_length, x.device)
+            scores = attn_scores if block_idx > 1 else None
+            ops.attn_cache(q, att, self.k_cache, self.v_cache, plan, cap, scores, 1.0 / (block_m * n_heads),
+                           n_heads, max_length, softmax_scale)
+
+    att = self.attn_out(att)
+    x = x + self.dropout(att)
+    og_x = x
+    h = _norm(self.ff_norm, x)
+    h, h_up = self.ff_proj(h), self.up_proj(h)
+    h = self.act(h) * h_up
+    h = self.ff_out(h)
+    h = self.dropout(h)
+    return (og_x + h).unsqueeze(0)
+
+
+def install_into_reference(modeling_module) -> None:
+    """Rebind the operator the reference model calls.
+
+    The reference imports the operator into ``llada/model/modeling_llada.py``
+    (line 55) and calls it from ``LLaDABlock.attention`` (line 760), so
+    replacing that module attribute routes every layer through this package.
+    """
+    modeling_module.flash_fused_elastic_cache = flash_fused_elastic_cache

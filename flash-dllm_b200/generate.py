@@ -1,0 +1,316 @@
+"""Flash-Cache / Flash-Verify decode driver (``generate_with_Flash_dLLM``).
+
+Same entry point, arguments and results as ``llada/generate.py:61-472``:
+continuous batching over ``batch_size`` sequence slots, a masked window of
+``block_length`` slots decoded by confidence (``threshold``), top-k selective
+refresh of the ``track_num * block_length`` highest-attention decoded slots
+plus ``mask_num - 1`` future windows, and with ``verify=True`` a second
+forward that checks up to ``block_length // 2`` drafts against their
+mask-view (acceptance prefix ``cumprod >= gamma``).
+
+What differs is how a step is executed.  Per-sequence host loops with
+``.item()`` syncs become batched device kernels (fp64 confidence
+statistics, window acceptance, verify acceptance scan, refresh sort) with at
+most three small device->host reads per step; the LM head runs only on the
+rows the step reads (masked rows; verify mask-view rows); KV caches are
+zero-initialised.  Sorting ties resolve in index order (the reference's
+``torch.sort`` is unstable).  Where the reference cannot continue -- a
+verify step whose masked window is cut short by the end of the slot buffer
+(generate.py:215 slices a full window and the assignment at :235 raises) --
+the actual window length is used.
+
+``min_keep`` (default 1, the reference) forces a minimum number of accepted
+tokens per step; ``trace`` (a list) receives the per-step decisions.
+"""
+from __future__ import annotations
+
+import time
+from typing import List, Optional
+
+import numpy as np
+import torch
+
+from . import ops
+
+
+def get_rotary_embedding(seq_len: int, dim: int, rope_theta: float, device=None):
+    """RoPE tables (generate.py:44-50): fp32 (sin, cos) of shape (seq_len, dim)."""
+    inv_freq = 1.0 / (rope_theta ** (torch.arange(0, dim, 2, device=device, dtype=torch.float32) / dim))
+    seq = torch.arange(seq_len, device=device, dtype=torch.float32)
+    freqs = torch.einsum("i , j -> i j", seq, inv_freq)
+    pos = torch.cat((freqs, freqs), dim=-1)
+    return pos.sin(), pos.cos()
+
+
+def make_blocks(j: int, seqlen_k, max_length, start_m: int, end_m: int, block_m: int, device=None):
+    """Block-table rows (seq, k_end, q_start, q_end) in ``block_m`` tiles (generate.py:52-58)."""
+    q_starts = torch.arange(start_m, end_m, block_m, device=device)
+    q_ends = q_starts + block_m
+    q_ends[-1] = end_m
+    return torch.stack((torch.full_like(q_starts, j), torch.full_like(q_starts, seqlen_k[j]), q_starts, q_ends), 1)
+
+
+def _tiles(rows: List, j: int, k_end: int, start: int, n: int, bm: int) -> None:
+    for s in range(start, start + n, bm):
+        rows.append((j, k_end, s, min(s + bm, start + n)))
+
+
+class _Slots:
+    """Host-side state of the sequence slots (the reference's per-slot lists)."""
+
+    def __init__(self, b: int):
+        self.active = [-1] * b
+        self.nd = [0] * b
+        self.pred = [0] * b
+        self.eos = [-1] * b
+        self.seqlen_k = [0] * b
+        self.masked = [None] * b
+        self.tracked = [None] * b
+
+
+@torch.no_grad()
+def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, responses, n_steps, steps=128,
+                             gen_length=128, block_length=128, temperature=0., remasking='low_confidence',
+                             mask_id=126336, threshold=0.9, gamma=0.9, track_num=4, mask_num=4, eos_id=126081,
+                             verify=False, sliding_window=True, is_instruct=True, tokenizer=None, stop_tokens=None,
+                             min_keep: int = 1, trace: Optional[list] = None, max_steps: Optional[int] = None,
+                             step_hook=None, record=None):
+    """Returns ``(responses, num_tokens, max_num_tokens)`` like the reference;
+    ``responses[i]`` is the decoded text (token ids when ``tokenizer`` is
+    None) and ``n_steps[i]`` counts the steps of prompt ``i``.  ``max_steps``
+    stops early (benchmarking); ``step_hook(step)`` runs after each step;
+    ``record(verify, x_query, query_pos, key_pos, logits, logit_rows,
+    attn_scores)`` sees every forward (tests replay it through the oracle)."""
+    dev = model.device
+    cfg = model.config
+    d_model, n_heads, n_layers = cfg.d_model, cfg.n_heads, cfg.n_layers
+    head_dim = d_model // n_heads
+    bm, bn = block_length, 128
+    L = ((max(prompt_lengths) + gen_length + bm) // bn + 1) * bn
+    B = batch_size
+    stop_tokens = stop_tokens or []
+    num_tokens = max_num_tokens = 0
+    x = torch.full((B * L,), mask_id, dtype=torch.long, device=dev)
+    x_draft = torch.full((B * L,), mask_id, dtype=torch.long, device=dev)
+    full_pos = torch.arange(B * L, device=dev).reshape(B, L)
+    attn_scores = torch.zeros(B * L, dtype=torch.float32, device=dev)
+    sin, cos = get_rotary_embedding(L, head_dim, cfg.rope_theta, dev)
+    rotary_emb_pos = [sin.repeat(B, 1).contiguous(), cos.repeat(B, 1).contiguous()]
+    for block in model.model.transformer.blocks:
+        block.k_cache = torch.zeros((L * B, d_model), dtype=model.dtype, device=dev)
+        block.v_cache = torch.zeros((L * B, d_model), dtype=model.dtype, device=dev)
+    empty_i32 = torch.tensor([], device=dev, dtype=torch.int32)
+    empty_i64 = torch.tensor([], device=dev, dtype=torch.int64)
+    masks = [torch.from_numpy(_verify_mask(bm, s)).to(dev) for s in range(bm // 2 + 1)]
+    ar_L = torch.arange(L, device=dev)
+    st = _Slots(B)
+    count = 0
+    start_layer = [-1] * B
+
+    def load(j: int, i: int) -> None:
+        p = prompt_lengths[i]
+        x[j * L:(j + 1) * L] = mask_id
+        x[j * L: j * L + p] = prompts[i].to(dev)
+        x[j * L + p + gen_length:(j + 1) * L] = eos_id
+        x_draft[j * L:(j + 1) * L] = mask_id
+        x_draft[j * L: j * L + p] = prompts[i].to(dev)
+        full_pos[j] = torch.arange(j * L, (j + 1) * L, device=dev)
+        st.active[j] = i
+        st.nd[j] = p
+        st.pred[j] = p + gen_length + j * L
+        st.eos[j] = -1
+        st.seqlen_k[j] = (p + gen_length) // bn * bn + bn
+        st.masked[j] = full_pos[j, p:p + bm]
+        st.tracked[j] = torch.cat([full_pos[j, :p], full_pos[j, p + bm:st.seqlen_k[j]]])
+        start_layer[j] = -1
+
+    for j in range(B):
+        if count < len(prompts):
+            load(j, count)
+            count += 1
+
+    step = 0
+    while True:
+        act = [j for j in range(B) if st.active[j] != -1]
+        if not act:
+            break
+        # ---------------------------------------------------- Flash-Cache --
+        m_rows, t_rows, acc = [], [], 0
+        m_lens = []
+        for j in act:
+            n = st.masked[j].numel()
+            m_lens.append(n)
+            if n:
+                _tiles(m_rows, j, st.seqlen_k[j], acc, n, bm)
+                acc += n
+        r_m = acc
+        for j in act:
+            n = st.tracked[j].numel()
+            if n:
+                _tiles(t_rows, j, st.seqlen_k[j], acc, n, bm)
+                acc += n
+        tables = torch.tensor(m_rows + t_rows, dtype=torch.int64).reshape(-1, 4).to(dev, non_blocking=True)
+        masked_blocks = tables[:len(m_rows)] if m_rows else empty_i32
+        tracked_blocks = tables[len(m_rows):] if t_rows else empty_i32
+        query_pos_flat = torch.cat([st.masked[j] for j in act] + [st.tracked[j] for j in act])
+        x_query = x[query_pos_flat]
+        positions = [query_pos_flat, empty_i64, rotary_emb_pos, [], attn_scores, []]
+        lengths = [start_layer, None, masked_blocks, tracked_blocks, tables, st.active, len(m_rows), L, bm, bn,
+                   None, False]
+        logits = model(x_query.unsqueeze(0), use_cache=True, lengths=lengths, positions=positions,
+                       logit_rows=r_m).logits[0]
+        if record is not None:
+            record(False, x_query, query_pos_flat, None, logits, torch.arange(r_m, device=dev), attn_scores)
+        p_max, x0, _ = ops.row_stats(logits)
+        info = np.zeros((len(act), 4), np.int64)
+        off = 0
+        for k, j in enumerate(act):
+            info[k] = (off, m_lens[k], j * L + st.nd[j], st.pred[j])
+            off += m_lens[k]
+        seq_info = torch.from_numpy(info).to(dev, non_blocking=True)
+        eos_known = torch.tensor([1 if st.eos[j] != -1 else 0 for j in act], dtype=torch.int32).to(dev)
+        keep_d, len_d, eos_d = ops.window_accept(p_max, x0, query_pos_flat[:r_m], seq_info, eos_known, L, threshold,
+                                                 min_keep, eos_id, full_pos, x, x_draft if verify else None)
+        host = torch.cat([keep_d.long(), len_d.long(), eos_d]).cpu().tolist()  # one device->host read
+        na = len(act)
+        keep1, lnum, eos1 = host[:na], host[na:2 * na], host[2 * na:]
+        for k, j in enumerate(act):
+            st.nd[j] += keep1[k]
+            if st.eos[j] == -1 and eos1[k] >= 0:
+                st.eos[j] = eos1[k]
+                st.pred[j] = eos1[k] + 1
+        rec = {"keep": dict(zip(act, keep1))}
+
+        # --------------------------------------------------- Flash-Verify --
+        if verify:
+            s_list = [min(max(lnum[k] - keep1[k], 0), bm // 2) for k in range(len(act))]
+            q_parts, k_parts, draft_parts, vrows, draft_flag, logit_idx = [], [], [], [], [], []
+            acc_q = acc_k = 0
+            for k, j in enumerate(act):
+                s = s_list[k]
+                t = 2 * bm - 2 * s
+                nd = st.nd[j]
+                tr = full_pos[j, nd - t:nd]
+                dr = full_pos[j, nd:nd + s]
+                q_parts += [tr, dr, dr]
+                k_parts += [full_pos[j, :nd - t], full_pos[j, nd + s:st.seqlen_k[j]]]
+                draft_parts.append(dr)
+                nq = tr.numel() + 2 * dr.numel()
+                nk = k_parts[-2].numel() + k_parts[-1].numel()
+                vrows.append((acc_k, acc_k + nk, acc_q, acc_q + nq))
+                draft_flag += [0] * tr.numel() + [1] * dr.numel() + [0] * dr.numel()
+                logit_idx += list(range(acc_q + tr.numel() + dr.numel(), acc_q + nq))
+                acc_q += nq
+                acc_k += nk
+            qpos = torch.cat(q_parts)
+            key_pos_flat = torch.cat(k_parts)
+            flag = torch.tensor(draft_flag, dtype=torch.bool).to(dev, non_blocking=True)
+            x_verify = torch.where(flag, x_draft[qpos], x[qpos])
+            attn_mask = torch.cat([masks[s] for s in s_list])
+            vblocks = torch.tensor(vrows, dtype=torch.int32).to(dev, non_blocking=True)
+            lidx = torch.tensor(logit_idx, dtype=torch.int64).to(dev, non_blocking=True)
+            positions = [qpos, key_pos_flat, rotary_emb_pos, [], attn_scores, attn_mask]
+            lengths = [start_layer, vblocks, None, tracked_blocks, None, st.active, len(m_rows), L, bm, bn, None,
+                       True]
+            draft_slots = torch.cat(draft_parts) if draft_parts else empty_i64
+            if sum(s_list) > 0:
+                logits_v = model(x_verify.unsqueeze(0), use_cache=True, lengths=lengths, positions=positions,
+                                 logit_rows=lidx).logits[0]
+                if record is not None:
+                    record(True, x_verify, qpos, key_pos_flat, logits_v, lidx, attn_scores)
+                draft_tok = x_draft[draft_slots]
+                _, _, p_tok = ops.row_stats(logits_v, draft_tok)
+            else:
+                # No sequence has a draft to check: the verify forward would write
+                # nothing (no cache, no scores) and none of its logits are read.
+                if record is not None:
+                    record(True, x_verify, qpos, key_pos_flat, None, lidx, attn_scores)
+                draft_tok = draft_slots
+                p_tok = torch.zeros(0, dtype=torch.float64, device=dev)
+            info2 = np.zeros((len(act), 4), np.int64)
+            o2 = 0
+            for k, j in enumerate(act):
+                info2[k] = (o2, s_list[k], 0, st.pred[j])
+                o2 += s_list[k]
+            eos_known = torch.tensor([1 if st.eos[j] != -1 else 0 for j in act], dtype=torch.int32).to(dev)
+            keep2_d, eos2_d = ops.verify_accept(p_tok, draft_tok, draft_slots, torch.from_numpy(info2).to(dev),
+                                                eos_known, gamma, eos_id, x)
+            host = torch.cat([keep2_d.long(), eos2_d]).cpu().tolist()
+            keep2, eos2 = host[:len(act)], host[len(act):]
+            for k, j in enumerate(act):
+                st.nd[j] += keep2[k]
+                if st.eos[j] == -1 and eos2[k] >= 0:
+                    st.eos[j] = eos2[k]
+                    st.pred[j] = eos2[k] + 1
+            last_keep = keep2
+            rec.update(verify_s=dict(zip(act, s_list)), verify_keep=dict(zip(act, keep2)))
+        else:
+            last_keep = keep1
+
+        for j in act:
+            n_steps[st.active[j]] += 1
+
+        # -------------------------------------------- refresh / finish --
+        nd_t = torch.tensor([st.nd[j] for j in act], dtype=torch.int64).to(dev)
+        pred_t = torch.tensor([st.pred[j] for j in act], dtype=torch.int64).to(dev)
+        rows = full_pos[act]
+        cont = ((ar_L[None, :] >= nd_t[:, None]) & (rows < pred_t[:, None])).any(1).cpu().tolist()
+        counts = np.zeros(B, np.int64)
+        for k, j in enumerate(act):
+            if cont[k]:
+                counts[j] = st.nd[j] - last_keep[k]
+        ops.refresh_sort(full_pos, torch.from_numpy(counts).to(dev), attn_scores)
+        for k, j in enumerate(act):
+            nd = st.nd[j]
+            if cont[k]:
+                st.masked[j] = full_pos[j, nd:nd + bm]
+                if track_num < 0:
+                    st.tracked[j] = torch.cat([full_pos[j, :nd], full_pos[j, nd + bm:st.seqlen_k[j]]])
+                else:
+                    t0 = max(0, nd - track_num * bm)
+                    t1 = min(st.seqlen_k[j], nd + bm * mask_num)
+                    st.tracked[j] = torch.cat([full_pos[j, t0:nd], full_pos[j, nd + bm:t1]])
+                start_layer[j] = n_layers
+            else:
+                i = st.active[j]
+                ids = x[j * L + prompt_lengths[i]: j * L + nd].tolist()
+                if tokenizer is not None:
+                    text = tokenizer.decode(ids, skip_special_tokens=False)
+                    for stop_seq in stop_tokens:
+                        if stop_seq in text:
+                            text = text.split(stop_seq)[0]
+                    ids2 = torch.tensor(tokenizer(text)["input_ids"])
+                    responses[i] = tokenizer.decode(ids2, skip_special_tokens=True)
+                else:
+                    responses[i] = ids
+                num_tokens += nd - prompt_lengths[i]
+                max_num_tokens += gen_length
+                if count < len(prompts):
+                    load(j, count)
+                    count += 1
+                else:
+                    st.active[j] = -1
+                    st.masked[j] = empty_i64
+                    st.tracked[j] = empty_i64
+        if trace is not None:
+            rec["nd"] = list(st.nd)
+            trace.append(rec)
+        attn_scores.zero_()
+        step += 1
+        if step_hook is not None:
+            step_hook(step)
+        if max_steps is not None and step >= max_steps:
+            break
+    return responses, num_tokens, max_num_tokens
+
+
+def _verify_mask(bm: int, s: int) -> np.ndarray:
+    """(2bm, 2bm) bool verify mask for S drafts (generate.py:262-269)."""
+    t = 2 * bm - 2 * s
+    m = np.ones((2 * bm, 2 * bm), dtype=np.bool_)
+    i = np.arange(s)
+    m[:t, t:t + s] = False
+    blk = np.block([[i[:, None] >= i[None, :], i[:, None] < i[None, :]],
+                    [i[:, None] > i[None, :], i[:, None] <= i[None, :]]])
+    m[t:t + 2 * s, t:t + 2 * s] = blk
+    return m

@@ -175,3 +175,59 @@ def verify_attn(q1, k1, v1, o, k_cache, v_cache, pos_k, attn_mask, verify_blocks
     call("fdllm_verify_attn", ptr(q1), ptr(k1), ptr(v1), ptr(o), ptr(k_cache), ptr(v_cache), ptr(pos_k), n_pos,
          ptr(mask), ptr(vb), nb, block_rows, q1.shape[0], d_model, n_heads, k_cache.shape[0], float(softmax_scale),
          kv_splits, ptr(ws), ws.numel(), _stream())
+
+
+# ------------------------------------------------------------- decoding --
+
+def row_stats(logits: torch.Tensor, tokens: Optional[torch.Tensor] = None):
+    """fp64 softmax max-probability and first argmax of each logit row, and
+    the probability of ``tokens[r]`` when given -> (p_max, argmax, p_tok)."""
+    if logits.dim() != 2 or logits.dtype != BF16 or logits.stride(1) != 1:
+        raise ValueError("logits must be a 2-D bf16 tensor with unit column stride")
+    n, v = logits.shape
+    dev = logits.device
+    p = torch.empty(n, dtype=torch.float64, device=dev)
+    am = torch.empty(n, dtype=torch.int64, device=dev)
+    pt = None
+    if tokens is not None:
+        tokens = tokens.to(torch.int64).contiguous()
+        pt = torch.empty(n, dtype=torch.float64, device=dev)
+    call("fdllm_row_stats", ptr(logits), logits.stride(0), n, v, ptr(tokens), ptr(p), ptr(am), ptr(pt), _stream())
+    return p, am, pt
+
+
+def window_accept(p, tok, window, seq_info, eos_known, lmax: int, threshold: float, min_keep: int, eos_id: int,
+                  full_pos, x, x_draft=None):
+    """Batched confidence acceptance; ``seq_info`` int64 (B, 4) = (row offset,
+    window length, flat full_pos index of num_decoded, predicted_length).
+    Returns device (keep int32, length_num int32, eos_slot int64)."""
+    b = seq_info.shape[0]
+    dev = p.device
+    keep = torch.empty(b, dtype=torch.int32, device=dev)
+    length = torch.empty(b, dtype=torch.int32, device=dev)
+    eos = torch.empty(b, dtype=torch.int64, device=dev)
+    call("fdllm_window_accept", ptr(p), ptr(tok), ptr(window), ptr(seq_info), ptr(eos_known), b,
+         full_pos.shape[0], lmax,
+         float(threshold), int(min_keep), int(eos_id), ptr(full_pos), ptr(x), ptr(x_draft), ptr(keep), ptr(length),
+         ptr(eos), _stream())
+    return keep, length, eos
+
+
+def verify_accept(p, draft_tok, draft_slot, seq_info, eos_known, gamma: float, eos_id: int, x):
+    """Batched Flash-Verify acceptance scan -> device (keep int32, eos_slot int64)."""
+    b = seq_info.shape[0]
+    dev = seq_info.device
+    keep = torch.empty(b, dtype=torch.int32, device=dev)
+    eos = torch.empty(b, dtype=torch.int64, device=dev)
+    call("fdllm_verify_accept", ptr(p), ptr(draft_tok), ptr(draft_slot), ptr(seq_info), ptr(eos_known), b,
+         x.numel(), float(gamma), int(eos_id), ptr(x), ptr(keep), ptr(eos), _stream())
+    return keep, eos
+
+
+def refresh_sort(full_pos: torch.Tensor, counts: torch.Tensor, scores: torch.Tensor) -> None:
+    """In place: full_pos[j, :counts[j]] ordered by ascending score (stable)."""
+    _check(full_pos, "full_pos", torch.int64, 2)
+    _check(scores, "scores", torch.float32)
+    counts = counts.to(torch.int64).contiguous()
+    call("fdllm_refresh_sort", ptr(full_pos), full_pos.shape[0], full_pos.shape[1], ptr(counts), ptr(scores),
+         scores.numel(), _stream())

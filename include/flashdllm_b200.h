@@ -130,6 +130,46 @@ int fdllm_verify_attn(const void* q1, const void* k1, const void* v1, void* o, c
                       int32_t d_model, int32_t n_heads, int64_t n_slots, float softmax_scale, int32_t kv_splits,
                       void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* fp64 softmax statistics of logit rows (bf16 [n_rows, ld], vocab used columns): for row r
+ * p_max[r] = max_v softmax(row)_v computed in fp64, argmax[r] = first index of the maximum, and
+ * when p_tok != NULL, p_tok[r] = softmax(row)[tokens[r]].
+ * ref llada/generate.py:218-219, 320-321, 337-338 (F.softmax(logits.to(float64)) + max / gather). */
+int fdllm_row_stats(const void* logits, int64_t ld, int32_t n_rows, int32_t vocab, const int64_t* tokens,
+                    double* p_max, int64_t* argmax, double* p_tok, cudaStream_t stream);
+
+/* Confidence acceptance of the masked window, batched over sequences (one warp each).
+ * full_pos is int64 [batch_slots, lmax]; x and x_draft hold batch_slots * lmax tokens.
+ * seq_info int64 [batch, 4] = (row offset into p/tok/window, window length n <= 256, flat index
+ * slot * lmax + num_decoded into full_pos, predicted_length as a flat slot).  For sequence j:
+ * probabilities of window slots >= predicted_length are zeroed
+ * when eos_known[j]; the window is ordered by descending probability (ties keep window order);
+ * keep = min(n, max(#(p >= threshold), min_keep)); full_pos row at the given flat index receives
+ * the ordered window slots;
+ * x[slot] = token for the first keep slots; x_draft[slot] = token for every window slot when
+ * x_draft != NULL.  Outputs keep_out, length_out (slots before predicted_length) and eos_out (largest
+ * committed slot holding eos_id, else -1).
+ * ref llada/generate.py:215-251 (verify stage 1) and :335-361 (Flash-Cache acceptance). */
+int fdllm_window_accept(const double* p, const int64_t* tok, const int64_t* window, const int64_t* seq_info,
+                        const int32_t* eos_known, int32_t batch, int64_t batch_slots, int64_t lmax, double threshold,
+                        int32_t min_keep, int64_t eos_id, int64_t* full_pos, int64_t* x, int64_t* x_draft,
+                        int32_t* keep_out, int32_t* length_out, int64_t* eos_out, cudaStream_t stream);
+
+/* Flash-Verify acceptance scan, batched over sequences.  seq_info int64 [batch, 4] = (row offset
+ * into p/draft_tok/draft_slot, number of drafts S, unused, predicted_length); x holds n_slots tokens.  p[i] is the
+ * mask-view probability of draft i; drafts at slots >= predicted_length count as 0 when
+ * eos_known[j]; keep = #(cumprod(p) >= gamma) with the product taken sequentially; the first keep
+ * drafts are committed to x.  ref llada/generate.py:312-333, 352-361. */
+int fdllm_verify_accept(const double* p, const int64_t* draft_tok, const int64_t* draft_slot,
+                        const int64_t* seq_info, const int32_t* eos_known, int32_t batch, int64_t n_slots,
+                        double gamma, int64_t eos_id, int64_t* x, int32_t* keep_out, int64_t* eos_out,
+                        cudaStream_t stream);
+
+/* Top-k selective refresh order: for each sequence j, stably sort full_pos[j, 0:counts[j]]
+ * (int64 [batch, lmax]) ascending by scores[full_pos[j, i]] in place (counts[j] <= 8192).
+ * ref llada/generate.py:364-366. */
+int fdllm_refresh_sort(int64_t* full_pos, int32_t batch, int64_t lmax, const int64_t* counts, const float* scores,
+                       int64_t n_slots, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

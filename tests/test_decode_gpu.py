@@ -1,0 +1,147 @@
+"""GPU parity of the decode bookkeeping kernels against the oracle's decision
+functions (restating llada/generate.py).  Integer decisions are compared
+bit-exactly given identical probabilities / scores, including ties (the
+oracle sorts stably, like the kernels); fp64 probabilities to 1e-12."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import decode_oracle as do
+
+pytestmark = pytest.mark.gpu
+
+
+def test_row_stats_matches_fp64_softmax_with_ties():
+    import flash_dllm_b200.ops as ops
+    g = torch.Generator().manual_seed(0)
+    R, V = 37, 126464
+    logits = (torch.randn(R, V, generator=g) * 3).bfloat16()
+    logits[0, 5] = logits[0, 77] = 40.0      # tie at the maximum: lowest id wins
+    logits[1] = 0.0                          # all equal
+    tok = torch.randint(0, V, (R,), generator=g)
+    p, am, pt = ops.row_stats(logits.cuda(), tok.cuda())
+    po, amo = do.confidence(logits)
+    pto = do.token_prob(logits, tok)
+    assert torch.equal(am.cpu(), amo)
+    assert int(am[0]) == 5 and int(am[1]) == 0
+    assert torch.allclose(p.cpu(), po, rtol=1e-12, atol=0)
+    assert torch.allclose(pt.cpu(), pto, rtol=1e-12, atol=1e-300)
+
+
+def _accept_case(seed, B, bm, L):
+    rs = np.random.RandomState(seed)
+    rows, info, window, eos_known, lens = [], [], [], [], []
+    off = 0
+    for j in range(B):
+        n = bm if j % 3 else max(1, bm - 5)   # some windows cut short
+        nd = rs.randint(0, L - n)
+        slots = j * L + nd + np.arange(n)
+        # probabilities with repeated values (ties) and some above the threshold
+        p = rs.choice([0.05, 0.5, 0.9, 0.95, 0.95, 0.2], n)
+        pred = j * L + nd + rs.randint(0, n + 1)
+        info.append((off, n, j * L + nd, pred))
+        eos_known.append(j % 2)
+        rows.append(p)
+        window.append(slots)
+        lens.append(n)
+        off += n
+    return (np.concatenate(rows), np.concatenate(window), np.array(info, np.int64), np.array(eos_known, np.int32),
+            lens)
+
+
+@pytest.mark.parametrize("min_keep,with_draft", [(1, False), (1, True), (2, False)])
+def test_window_accept_matches_oracle(min_keep, with_draft):
+    import flash_dllm_b200.ops as ops
+    B, bm, L, eos_id, thr = 9, 32, 256, 7, 0.9
+    p, window, info, eos_known, lens = _accept_case(3, B, bm, L)
+    rs = np.random.RandomState(4)
+    tok = rs.randint(0, 10, p.shape[0]).astype(np.int64)
+    dev = torch.device("cuda")
+    full_pos = torch.arange(B * L, device=dev).reshape(B, L)
+    fp_ref = full_pos.cpu().clone()
+    x = torch.full((B * L,), -1, dtype=torch.int64, device=dev)
+    x_ref = x.cpu().clone()
+    xd = torch.full((B * L,), -1, dtype=torch.int64, device=dev) if with_draft else None
+    keep, length, eos = ops.window_accept(torch.from_numpy(p).to(dev), torch.from_numpy(tok).to(dev),
+                                          torch.from_numpy(window).to(dev), torch.from_numpy(info).to(dev),
+                                          torch.from_numpy(eos_known).to(dev), L, thr, min_keep, eos_id, full_pos,
+                                          x, xd)
+    for j in range(B):
+        off, n, at, pred = (int(v) for v in info[j])
+        pj = torch.from_numpy(p[off:off + n]).clone()
+        slots = torch.from_numpy(window[off:off + n])
+        tail = slots >= pred
+        if eos_known[j]:
+            pj[tail] = 0
+        order = do.sort_desc_stable(pj)
+        k = min(do.accept_count(pj, thr, min_keep), n)
+        assert int(keep[j]) == k
+        assert int(length[j]) == (n - int(tail.sum()) if eos_known[j] else n)
+        nd = at % L
+        fp_ref[j, nd:nd + n] = slots[order]
+        x_ref[slots[order][:k]] = torch.from_numpy(tok[off:off + n])[order][:k]
+        committed = slots[order][:k][torch.from_numpy(tok[off:off + n])[order][:k] == eos_id]
+        assert int(eos[j]) == (int(committed.max()) if committed.numel() else -1)
+    assert torch.equal(full_pos.cpu(), fp_ref)
+    assert torch.equal(x.cpu(), x_ref)
+    if with_draft:
+        assert torch.equal(xd.cpu()[torch.from_numpy(window)], torch.from_numpy(tok))
+
+
+def test_verify_accept_matches_oracle():
+    import flash_dllm_b200.ops as ops
+    rs = np.random.RandomState(8)
+    B, gamma, eos_id = 10, 0.8, 3
+    s_list = [0, 16, 5, 1, 16, 9, 2, 16, 7, 4]
+    info, p, toks, slots = [], [], [], []
+    off = 0
+    for j, s in enumerate(s_list):
+        pv = rs.choice([1.0, 0.99, 0.95, 0.9, 0.5], s)
+        pred = 1000 * j + rs.randint(0, 20)
+        info.append((off, s, 0, pred))
+        p.append(pv)
+        toks.append(rs.randint(0, 6, s))
+        slots.append(1000 * j + np.arange(s) * 2)
+        off += s
+    eos_known = np.array([j % 2 for j in range(B)], np.int32)
+    p, toks, slots = (np.concatenate(a) for a in (p, toks, slots))
+    dev = torch.device("cuda")
+    x = torch.full((10000,), -1, dtype=torch.int64, device=dev)
+    keep, eos = ops.verify_accept(torch.from_numpy(p).to(dev), torch.from_numpy(toks).to(dev),
+                                  torch.from_numpy(slots).to(dev), torch.from_numpy(np.array(info)).to(dev),
+                                  torch.from_numpy(eos_known).to(dev), gamma, eos_id, x)
+    xr = torch.full((10000,), -1, dtype=torch.int64)
+    for j, s in enumerate(s_list):
+        off, _, _, pred = info[j]
+        pv = torch.from_numpy(p[off:off + s]).clone()
+        sl = torch.from_numpy(slots[off:off + s])
+        if eos_known[j]:
+            pv[sl >= pred] = 0
+        k = do.verify_keep(pv, gamma)
+        assert int(keep[j]) == k, j
+        tk = torch.from_numpy(toks[off:off + s])
+        xr[sl[:k]] = tk[:k]
+        e = sl[:k][tk[:k] == eos_id]
+        assert int(eos[j]) == (int(e.max()) if e.numel() else -1)
+    assert torch.equal(x.cpu(), xr)
+
+
+@pytest.mark.parametrize("n_max", [40, 896, 2176])
+def test_refresh_sort_matches_stable_oracle(n_max):
+    import flash_dllm_b200.ops as ops
+    rs = np.random.RandomState(n_max)
+    B, L = 5, max(n_max, 64) + 64
+    scores = rs.choice([-1.5, 0.0, -0.0, 0.25, 3.0], B * L).astype(np.float32)
+    scores[::7] = rs.standard_normal(len(scores[::7]))
+    full_pos = np.stack([j * L + rs.permutation(L) for j in range(B)]).astype(np.int64)
+    counts = np.array([n_max, 0, 1, n_max // 2, rs.randint(2, n_max)], np.int64)
+    dev = torch.device("cuda")
+    fp = torch.from_numpy(full_pos).to(dev)
+    ops.refresh_sort(fp, torch.from_numpy(counts).to(dev), torch.from_numpy(scores).to(dev))
+    ref = torch.from_numpy(full_pos).clone()
+    sc = torch.from_numpy(scores)
+    for j in range(B):
+        n = int(counts[j])
+        head = ref[j, :n]
+        ref[j, :n] = head[do.refresh_order(sc[head])]
+    assert torch.equal(fp.cpu(), ref)

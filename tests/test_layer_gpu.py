@@ -1,0 +1,102 @@
+"""The drop-in layer operator on the GPU against the oracle layer driver
+(reference semantics, bf16 rounding points) for both modes: block output,
+cache rows written and the accumulated attention scores."""
+import pytest
+import torch
+
+import cases
+from oracle import decode_oracle as do
+from oracle import flash_cache_oracle as fco
+from oracle import tiny_model as tm
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _rel(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-6)).item()
+
+
+def _blocks(d_model=1024, n_heads=8, hidden=2048):
+    from flash_dllm_b200.model import LLaDABlockB200, LLaDAConfigB200
+    tc = tm.TinyConfig(d_model=d_model, n_heads=n_heads, n_layers=1, mlp_hidden_size=hidden, vocab_size=64,
+                       init_std=0.05)
+    w = tm.make_weights(tc, 5)
+    cpu = tm.TinyLLaDA(tc, w, dtype=torch.bfloat16).layers[0]
+    gpu = LLaDABlockB200(LLaDAConfigB200(d_model=d_model, n_heads=n_heads, n_layers=1, mlp_hidden_size=hidden,
+                                         vocab_size=64), 0, device="cuda", dtype=torch.bfloat16)
+    sd = {k[len("model.transformer.blocks.0."):]: v.bfloat16() for k, v in w.items()
+          if k.startswith("model.transformer.blocks.0.")}
+    gpu.load_state_dict(sd, strict=True)
+    return cpu, gpu
+
+
+def test_layer_flash_cache_mode():
+    from flash_dllm_b200.flash_cache import flash_fused_elastic_cache
+    d, H, bm, L, B = 1024, 8, 32, 384, 3
+    cpu, gpu = _blocks(d, H)
+    g = torch.Generator().manual_seed(1)
+    masked_counts, tracked_counts, seqlen_k = [32, 32, 32], [64, 5, 0], [384, 256, 128]
+    mb, tb = do.build_block_tables(masked_counts, tracked_counts, seqlen_k, bm)
+    pos = []
+    for j in range(B):
+        perm = torch.randperm(seqlen_k[j], generator=g)[:masked_counts[j] + tracked_counts[j]] + j * L
+        pos.append(perm)
+    pos_flat = torch.cat([p[:masked_counts[j]] for j, p in enumerate(pos)] +
+                         [p[masked_counts[j]:] for j, p in enumerate(pos)])
+    n = pos_flat.numel()
+    x = torch.randn(n, d, generator=g).bfloat16()
+    kc = torch.randn(B * L, d, generator=g).bfloat16()
+    vc = torch.randn(B * L, d, generator=g).bfloat16()
+    sin, cos = do.get_rotary_embedding(L, 128, 500000.0)
+    rot = [sin.repeat(B, 1), cos.repeat(B, 1)]
+    qb = torch.cat([mb, tb])
+
+    def run(block, dev, scores):
+        block.k_cache, block.v_cache = kc.to(dev).clone(), vc.to(dev).clone()
+        positions = [pos_flat.to(dev), torch.tensor([], dtype=torch.int64, device=dev),
+                     [t.to(dev) for t in rot], [], scores, []]
+        lengths = [[-1] * B, None, mb.to(dev), tb.to(dev), qb.to(dev), list(range(B)), mb.shape[0], L, bm, 128, None,
+                   False]
+        return block, positions, lengths
+
+    s_cpu = torch.zeros(B * L)
+    blk, positions, lengths = run(cpu, "cpu", s_cpu)
+    y_ref = fco.flash_fused_elastic_cache(blk, x, 2, positions, lengths).squeeze(0)
+    s_gpu = torch.zeros(B * L, device="cuda")
+    blk2, positions, lengths = run(gpu, "cuda", s_gpu)
+    y = flash_fused_elastic_cache(blk2, x.cuda(), 2, positions, lengths).squeeze(0)
+    assert _rel(y, y_ref) <= TOL
+    assert _rel(blk2.k_cache[pos_flat.cuda()], cpu.k_cache[pos_flat]) <= TOL
+    assert _rel(blk2.v_cache[pos_flat.cuda()], cpu.v_cache[pos_flat]) <= TOL
+    assert _rel(s_gpu, s_cpu) <= 1e-2
+    # layers 0 and 1 do not accumulate scores (flash_cache_triton.py:614)
+    s0 = torch.zeros(B * L, device="cuda")
+    blk2, positions, lengths = run(gpu, "cuda", s0)
+    flash_fused_elastic_cache(blk2, x.cuda(), 1, positions, lengths)
+    assert not s0.any()
+
+
+def test_layer_flash_verify_mode():
+    from flash_dllm_b200.flash_cache import flash_fused_elastic_cache
+    c = cases.verify_case()
+    d, H = cases.D_MODEL, cases.N_HEADS
+    cpu, gpu = _blocks(d, H, 512)
+    x = c["xn"].bfloat16()
+    kc, vc = c["k_cache"].bfloat16(), c["v_cache"].bfloat16()
+
+    def run(block, dev):
+        block.k_cache, block.v_cache = kc.to(dev).clone(), vc.to(dev).clone()
+        positions = [c["pos"].to(dev), c["pos_k"].to(dev), [c["sin"].to(dev), c["cos"].to(dev)], [],
+                     torch.zeros(2 * cases.LMAX, device=dev), c["attn_mask"].to(dev)]
+        lengths = [[-1, -1], c["blocks"].to(dev), None, torch.tensor([], dtype=torch.int32, device=dev), None, [0, 1],
+                   2, cases.LMAX, cases.BLOCK_M, 128, None, True]
+        return positions, lengths
+
+    positions, lengths = run(cpu, "cpu")
+    y_ref = fco.flash_fused_elastic_cache(cpu, x, 3, positions, lengths).squeeze(0)
+    positions, lengths = run(gpu, "cuda")
+    y = flash_fused_elastic_cache(gpu, x.cuda(), 3, positions, lengths).squeeze(0)
+    assert _rel(y, y_ref) <= TOL
+    assert torch.equal(gpu.k_cache.cpu(), kc)  # verify never writes the cache
