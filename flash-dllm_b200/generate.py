@@ -24,7 +24,6 @@ tokens per step; ``trace`` (a list) receives the per-step decisions.
 """
 from __future__ import annotations
 
-import time
 from typing import List, Optional
 
 import numpy as np
@@ -74,15 +73,29 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                              mask_id=126336, threshold=0.9, gamma=0.9, track_num=4, mask_num=4, eos_id=126081,
                              verify=False, sliding_window=True, is_instruct=True, tokenizer=None, stop_tokens=None,
                              min_keep: int = 1, trace: Optional[list] = None, max_steps: Optional[int] = None,
-                             step_hook=None, record=None):
+                             step_hook=None, record=None, stats: Optional[dict] = None):
     """Returns ``(responses, num_tokens, max_num_tokens)`` like the reference;
     ``responses[i]`` is the decoded text (token ids when ``tokenizer`` is
     None) and ``n_steps[i]`` counts the steps of prompt ``i``.  ``max_steps``
     stops early (benchmarking); ``step_hook(step)`` runs after each step;
     ``record(verify, x_query, query_pos, key_pos, logits, logit_rows,
-    attn_scores)`` sees every forward (tests replay it through the oracle)."""
+    attn_scores)`` sees every forward (tests replay it through the oracle);
+    ``stats`` (a dict) accumulates ``h2d_bytes`` / ``d2h_bytes`` / ``steps``."""
     dev = model.device
     cfg = model.config
+    io = stats if stats is not None else {}
+    io.setdefault("h2d_bytes", 0)
+    io.setdefault("d2h_bytes", 0)
+    io.setdefault("steps", 0)
+
+    def h2d(t: torch.Tensor) -> torch.Tensor:
+        io["h2d_bytes"] += t.numel() * t.element_size()
+        return t.pin_memory().to(dev, non_blocking=True) if t.device.type == "cpu" else t
+
+    def d2h(t: torch.Tensor) -> list:
+        io["d2h_bytes"] += t.numel() * t.element_size()
+        return t.cpu().tolist()
+
     d_model, n_heads, n_layers = cfg.d_model, cfg.n_heads, cfg.n_layers
     head_dim = d_model // n_heads
     bm, bn = block_length, 128
@@ -110,10 +123,11 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
     def load(j: int, i: int) -> None:
         p = prompt_lengths[i]
         x[j * L:(j + 1) * L] = mask_id
-        x[j * L: j * L + p] = prompts[i].to(dev)
+        prompt = h2d(prompts[i]) if prompts[i].device.type == "cpu" else prompts[i]
+        x[j * L: j * L + p] = prompt
         x[j * L + p + gen_length:(j + 1) * L] = eos_id
         x_draft[j * L:(j + 1) * L] = mask_id
-        x_draft[j * L: j * L + p] = prompts[i].to(dev)
+        x_draft[j * L: j * L + p] = prompt
         full_pos[j] = torch.arange(j * L, (j + 1) * L, device=dev)
         st.active[j] = i
         st.nd[j] = p
@@ -149,7 +163,7 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
             if n:
                 _tiles(t_rows, j, st.seqlen_k[j], acc, n, bm)
                 acc += n
-        tables = torch.tensor(m_rows + t_rows, dtype=torch.int64).reshape(-1, 4).to(dev, non_blocking=True)
+        tables = h2d(torch.tensor(m_rows + t_rows, dtype=torch.int64).reshape(-1, 4))
         masked_blocks = tables[:len(m_rows)] if m_rows else empty_i32
         tracked_blocks = tables[len(m_rows):] if t_rows else empty_i32
         query_pos_flat = torch.cat([st.masked[j] for j in act] + [st.tracked[j] for j in act])
@@ -167,11 +181,11 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         for k, j in enumerate(act):
             info[k] = (off, m_lens[k], j * L + st.nd[j], st.pred[j])
             off += m_lens[k]
-        seq_info = torch.from_numpy(info).to(dev, non_blocking=True)
-        eos_known = torch.tensor([1 if st.eos[j] != -1 else 0 for j in act], dtype=torch.int32).to(dev)
+        seq_info = h2d(torch.from_numpy(info))
+        eos_known = h2d(torch.tensor([1 if st.eos[j] != -1 else 0 for j in act], dtype=torch.int32))
         keep_d, len_d, eos_d = ops.window_accept(p_max, x0, query_pos_flat[:r_m], seq_info, eos_known, L, threshold,
                                                  min_keep, eos_id, full_pos, x, x_draft if verify else None)
-        host = torch.cat([keep_d.long(), len_d.long(), eos_d]).cpu().tolist()  # one device->host read
+        host = d2h(torch.cat([keep_d.long(), len_d.long(), eos_d]))  # one device->host read
         na = len(act)
         keep1, lnum, eos1 = host[:na], host[na:2 * na], host[2 * na:]
         for k, j in enumerate(act):
@@ -204,11 +218,11 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                 acc_k += nk
             qpos = torch.cat(q_parts)
             key_pos_flat = torch.cat(k_parts)
-            flag = torch.tensor(draft_flag, dtype=torch.bool).to(dev, non_blocking=True)
+            flag = h2d(torch.tensor(draft_flag, dtype=torch.bool))
             x_verify = torch.where(flag, x_draft[qpos], x[qpos])
             attn_mask = torch.cat([masks[s] for s in s_list])
-            vblocks = torch.tensor(vrows, dtype=torch.int32).to(dev, non_blocking=True)
-            lidx = torch.tensor(logit_idx, dtype=torch.int64).to(dev, non_blocking=True)
+            vblocks = h2d(torch.tensor(vrows, dtype=torch.int32))
+            lidx = h2d(torch.tensor(logit_idx, dtype=torch.int64))
             positions = [qpos, key_pos_flat, rotary_emb_pos, [], attn_scores, attn_mask]
             lengths = [start_layer, vblocks, None, tracked_blocks, None, st.active, len(m_rows), L, bm, bn, None,
                        True]
@@ -232,10 +246,10 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
             for k, j in enumerate(act):
                 info2[k] = (o2, s_list[k], 0, st.pred[j])
                 o2 += s_list[k]
-            eos_known = torch.tensor([1 if st.eos[j] != -1 else 0 for j in act], dtype=torch.int32).to(dev)
-            keep2_d, eos2_d = ops.verify_accept(p_tok, draft_tok, draft_slots, torch.from_numpy(info2).to(dev),
+            eos_known = h2d(torch.tensor([1 if st.eos[j] != -1 else 0 for j in act], dtype=torch.int32))
+            keep2_d, eos2_d = ops.verify_accept(p_tok, draft_tok, draft_slots, h2d(torch.from_numpy(info2)),
                                                 eos_known, gamma, eos_id, x)
-            host = torch.cat([keep2_d.long(), eos2_d]).cpu().tolist()
+            host = d2h(torch.cat([keep2_d.long(), eos2_d]))
             keep2, eos2 = host[:len(act)], host[len(act):]
             for k, j in enumerate(act):
                 st.nd[j] += keep2[k]
@@ -251,15 +265,14 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
             n_steps[st.active[j]] += 1
 
         # -------------------------------------------- refresh / finish --
-        nd_t = torch.tensor([st.nd[j] for j in act], dtype=torch.int64).to(dev)
-        pred_t = torch.tensor([st.pred[j] for j in act], dtype=torch.int64).to(dev)
-        rows = full_pos[act]
-        cont = ((ar_L[None, :] >= nd_t[:, None]) & (rows < pred_t[:, None])).any(1).cpu().tolist()
+        ndp = h2d(torch.tensor([[st.nd[j] for j in act], [st.pred[j] for j in act], act], dtype=torch.int64))
+        rows = full_pos.index_select(0, ndp[2])
+        cont = d2h(((ar_L[None, :] >= ndp[0][:, None]) & (rows < ndp[1][:, None])).any(1))
         counts = np.zeros(B, np.int64)
         for k, j in enumerate(act):
             if cont[k]:
                 counts[j] = st.nd[j] - last_keep[k]
-        ops.refresh_sort(full_pos, torch.from_numpy(counts).to(dev), attn_scores)
+        ops.refresh_sort(full_pos, h2d(torch.from_numpy(counts)), attn_scores)
         for k, j in enumerate(act):
             nd = st.nd[j]
             if cont[k]:
@@ -273,7 +286,7 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                 start_layer[j] = n_layers
             else:
                 i = st.active[j]
-                ids = x[j * L + prompt_lengths[i]: j * L + nd].tolist()
+                ids = d2h(x[j * L + prompt_lengths[i]: j * L + nd])
                 if tokenizer is not None:
                     text = tokenizer.decode(ids, skip_special_tokens=False)
                     for stop_seq in stop_tokens:
@@ -297,6 +310,7 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
             trace.append(rec)
         attn_scores.zero_()
         step += 1
+        io["steps"] += 1
         if step_hook is not None:
             step_hook(step)
         if max_steps is not None and step >= max_steps:
