@@ -317,11 +317,15 @@ QkvPlan plan_qkv(int32_t n_rows, int32_t d_model, int32_t n_heads) {
   return pl;
 }
 
+// Workspace layout: a fixed counter region (so counters never move between
+// calls with different tile counts, and no call's partial sums land on another
+// call's counters), then the split-K partials.
+constexpr size_t kQkvCounterBytes = 4096;  // 1024 tiles; a K split is only used below ~2 x SM-count tiles
+
 size_t qkv_ws_bytes(const QkvPlan& pl) {
   if (pl.splits <= 1) return 256;
   const size_t tiles = static_cast<size_t>(pl.m_tiles) * pl.n_tiles;
-  const size_t counters = align_up(tiles * sizeof(int32_t), 256);
-  return counters + tiles * pl.splits * kQkvBM * pl.bn * sizeof(float);
+  return kQkvCounterBytes + tiles * pl.splits * kQkvBM * pl.bn * sizeof(float);
 }
 
 template <int BN>
@@ -377,10 +381,9 @@ int launch_qkv(const void* xn, const void* wq, const void* wk, const void* wv, c
   p.kb_per_split = pl.kb_per_split;
   p.m_tiles = pl.m_tiles;
   if (pl.splits > 1) {
-    const size_t tiles = static_cast<size_t>(pl.m_tiles) * pl.n_tiles;
+    if (static_cast<size_t>(pl.m_tiles) * pl.n_tiles * sizeof(int32_t) > kQkvCounterBytes) return FDLLM_ERR_ARG;
     p.counters = static_cast<int32_t*>(workspace);
-    p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
-                                          align_up(tiles * sizeof(int32_t), 256));
+    p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kQkvCounterBytes);
   }
   if (pl.bn == 128) return launch_qkv_bn<128>(mx, mq, mk, mv, p, pl, stream);
   return launch_qkv_bn<64>(mx, mq, mk, mv, p, pl, stream);
@@ -413,3 +416,4 @@ int fdllm_verify_qkv(const void* xn, const void* wq, const void* wk, const void*
 }
 
 }  // extern "C"
+

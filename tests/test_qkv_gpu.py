@@ -121,3 +121,22 @@ def test_rmsnorm_matches_reference_rounding(rows, dim):
     ref = fco.rms_norm(x, w, 1e-5)
     # identical rounding points; the fp32 sum order differs, so allow ~1 bf16 ulp
     assert _rel(y, ref) <= 8e-3
+
+
+def test_split_k_workspace_reuse_across_shapes():
+    """Split-K calls with different tile counts share one workspace: a call
+    with few tiles must not leave partial sums where a later call with more
+    tiles keeps its counters (all 96 head tiles of d_model 4096 checked)."""
+    import flash_dllm_b200.ops as ops
+    from flash_dllm_b200._lib import check_device_status
+    dev = torch.device("cuda")
+    for n_rows, d_model, n_slots in ((64, 1024, 256), (64, 4096, 512), (200, 1024, 512), (64, 4096, 512)):
+        n_heads = d_model // 128
+        x, w, pos, kc, vc, sin, cos = _case(n_rows, d_model, n_slots, seed=n_rows * 7 + d_model)
+        q = torch.empty(n_rows, d_model, dtype=torch.bfloat16, device=dev)
+        kd, vd = kc.to(dev), vc.to(dev)
+        ops.qkv_rope_cache(x.to(dev), *(t.to(dev) for t in w), pos.to(dev), sin.to(dev), cos.to(dev), q, kd, vd,
+                           n_heads)
+        check_device_status()
+        qo, ko, vo = _oracle(x, w, pos, kc, vc, sin, cos, n_heads)
+        assert _rel(q, qo) <= TOL and _rel(kd[pos.to(dev)], ko[pos]) <= TOL and _rel(vd[pos.to(dev)], vo[pos]) <= TOL
