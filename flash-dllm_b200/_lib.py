@@ -30,6 +30,7 @@ SIGNATURES = {
     "fdllm_rmsnorm": (_int, [_p, _p, _p, _i32, _i32, _f32, _p]),
     "fdllm_qkv_workspace_bytes": (_sz, [_i32, _i32, _i32]),
     "fdllm_qkv_rope_cache": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i64, _p, _sz, _p]),
+    "fdllm_qkv_rope_cache_noalloc": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i64, _p]),
     "fdllm_verify_qkv": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i64, _p, _sz, _p]),
     "fdllm_attn_plan_capacity": (_int, [_i32, _i32]),
     "fdllm_attn_plan_bytes": (_sz, [_i32, _i32]),

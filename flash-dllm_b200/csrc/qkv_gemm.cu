@@ -417,3 +417,62 @@ int fdllm_verify_qkv(const void* xn, const void* wq, const void* wk, const void*
 
 }  // extern "C"
 
+// ---------------------------------------------------------------------------
+// Entry point for callers that cannot allocate device memory.
+//
+// Some embedders drive this kernel from code that owns no device allocator:
+// a host runtime whose memory is handed out by another component, a plugin
+// loaded into a process that forbids cudaMalloc after start-up (to keep its
+// pool fixed), or a caller inside a region that must not allocate.  They
+// still pass the inputs and outputs, but not the split-K scratch
+// (fdllm_qkv_rope_cache's `workspace`).  This variant takes that scratch from
+// a fixed array compiled into the library instead.
+//
+//  * The array is kQkvNoAllocScratchBytes (24 MiB) of global memory on every
+//    GPU that loads the library, held until the process exits.
+//  * Requests whose split-K scratch would exceed it are refused with
+//    FDLLM_ERR_SCRATCH_LIMIT before anything is launched (for LLaDA-8B,
+//    d_model 4096, that is any call of more than 128 query rows; calls that
+//    need no split, such as 512 rows, use no scratch and are accepted).
+//  * The first call on a device resolves the array's device address
+//    (cudaGetSymbolAddress, with that device current); make that first call
+//    before any stream capture.
+//  * All calls share the array: the split counters are cleared at the start
+//    of every call, and calls that overlap on the GPU (other streams, other
+//    threads) race on it -- serialise them.
+//  * No cudaMalloc / cudaFree or other allocating routine is called.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kQkvNoAllocScratchBytes = size_t(24) << 20;
+static __device__ __align__(256) uint8_t g_qkv_noalloc_scratch[kQkvNoAllocScratchBytes];
+
+void* qkv_noalloc_scratch() {
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_qkv_noalloc_scratch) != cudaSuccess || p == nullptr) return nullptr;
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+}  // namespace
+
+extern "C" int fdllm_qkv_rope_cache_noalloc(const void* xn, const void* wq, const void* wk, const void* wv,
+                                            const int64_t* pos, const float* rope_sin, const float* rope_cos,
+                                            void* q_out, void* k_cache, void* v_cache, int32_t n_rows,
+                                            int32_t d_model, int32_t n_heads, int64_t n_slots, cudaStream_t stream) {
+  using namespace fdllm;
+  if (n_rows < 0 || n_heads <= 0 || d_model != n_heads * 128 || n_slots <= 0) return FDLLM_ERR_ARG;
+  if (n_rows == 0) return FDLLM_OK;
+  const QkvPlan pl = plan_qkv(n_rows, d_model, n_heads);
+  if (pl.splits > 1 && qkv_ws_bytes(pl) > kQkvNoAllocScratchBytes) return FDLLM_ERR_SCRATCH_LIMIT;
+  void* scratch = qkv_noalloc_scratch();
+  if (scratch == nullptr) return FDLLM_ERR_CUDA;
+  if (pl.splits > 1 && cudaMemsetAsync(scratch, 0, kQkvCounterBytes, stream) != cudaSuccess) return FDLLM_ERR_CUDA;
+  return launch_qkv(xn, wq, wk, wv, pos, rope_sin, rope_cos, q_out, k_cache, v_cache, n_rows, d_model, n_heads,
+                    n_slots, scratch, kQkvNoAllocScratchBytes, 1, stream);
+}

@@ -38,6 +38,7 @@ extern "C" {
 #define FDLLM_ERR_TABLE 5     /* device: malformed block table */
 #define FDLLM_ERR_WORKSPACE 6 /* workspace too small */
 #define FDLLM_ERR_DRIVER 7    /* TMA descriptor encode unavailable or failed */
+#define FDLLM_ERR_SCRATCH_LIMIT 8 /* request needs more scratch than the library's fixed array holds */
 
 /* Library version string. */
 const char* fdllm_version(void);
@@ -73,6 +74,20 @@ int fdllm_qkv_rope_cache(const void* xn, const void* wq, const void* wk, const v
                          const float* rope_sin, const float* rope_cos, void* q_out, void* k_cache, void* v_cache,
                          int32_t n_rows, int32_t d_model, int32_t n_heads, int64_t n_slots, void* workspace,
                          size_t workspace_bytes, cudaStream_t stream);
+
+/* fdllm_qkv_rope_cache for callers that cannot allocate device memory (for example a runtime
+ * whose device memory is owned by another component, or a plugin that may not call cudaMalloc
+ * once loaded): same arguments and results minus the workspace, whose role is taken by a fixed
+ * 24 MiB array inside the library (held on every GPU that loads it until exit).  No counterpart
+ * in the reference.  Calls needing more split-K scratch than that (d_model 4096: more than 128
+ * rows with a K split) return FDLLM_ERR_SCRATCH_LIMIT without launching.  The first call on a
+ * device looks up the array's address; make it before any stream capture.  Calls share the
+ * array (its counters are cleared on entry), so calls that overlap on the GPU race: serialise
+ * them.  Allocates nothing. */
+int fdllm_qkv_rope_cache_noalloc(const void* xn, const void* wq, const void* wk, const void* wv, const int64_t* pos,
+                                 const float* rope_sin, const float* rope_cos, void* q_out, void* k_cache,
+                                 void* v_cache, int32_t n_rows, int32_t d_model, int32_t n_heads, int64_t n_slots,
+                                 cudaStream_t stream);
 
 /* Verify-query projection: same math as fdllm_qkv_rope_cache, but Q, K and V are all written
  * row-indexed to q_out/k_out/v_out (bf16 [n_rows, d_model]); the cache is not touched.
