@@ -137,7 +137,7 @@ def _time_kernels(model, n_rows, batch, lmax, dev):
     scores = torch.zeros(batch * lmax, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2, rewritten between launches
 
-    def timed(fn, reps=10):
+    def timed(fn, reps=int(os.environ.get("BENCH_KERNEL_REPS", "10"))):
         ts = []
         for _ in range(reps + 2):
             flush.zero_()
@@ -271,9 +271,14 @@ def main():
     ap.add_argument("--impl", default="b200")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernels-only", type=int, default=0, metavar="SEQS",
+                    help="time only the hot kernels of one random LLaDA-8B layer at the step shape of SEQS "
+                         "sequences per GPU (small case for ncu captures)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.kernels_only:
+        return run_kernels_only(args.kernels_only)
     assert args.warmup >= 3, "at least 3 warm-up steps"
     world, rank, local = _dist()
     dev = torch.device("cuda", local)
@@ -398,6 +403,21 @@ def main():
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_kernels_only(seqs: int) -> None:
+    from types import SimpleNamespace
+    from flash_dllm_b200.model import LLaDABlockB200, LLaDAConfigB200
+    dev = torch.device("cuda", 0)
+    cfg = LLaDAConfigB200()
+    blk = LLaDABlockB200(cfg, 0, device=dev, dtype=torch.bfloat16)
+    g = torch.Generator(device=dev).manual_seed(0)
+    with torch.no_grad():
+        for name, p in blk.named_parameters():
+            p.fill_(1.0) if "norm" in name else p.normal_(0.0, 0.02, generator=g)
+    fake = SimpleNamespace(model=SimpleNamespace(transformer=SimpleNamespace(blocks=[blk])), config=cfg)
+    kt = _time_kernels(fake, 64 * seqs, seqs, WORKLOAD["seq_len"], dev)
+    print(json.dumps({k: v for k, v in kt.items()}), flush=True)
 
 
 def _count_launches(model, per, args):
