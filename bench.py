@@ -288,8 +288,10 @@ def main():
     cfg = LLaDAConfigB200()
     model = LLaDAModelB200.random_init(cfg, device=dev, seed=0)
     prompts = _prompts(WORKLOAD["global_batch"], cfg.vocab_size, cfg.mask_token_id)
-    per = WORKLOAD["global_batch"] // world
-    mine = prompts[rank * per:(rank + 1) * per]
+    from flash_dllm_b200.shard import reduce_counters, shard_range
+    s0, s1 = shard_range(WORKLOAD["global_batch"], rank, world)
+    mine = prompts[s0:s1]
+    per = len(mine)
     dist = None
     if world > 1:
         import torch.distributed as dist
@@ -351,16 +353,8 @@ def main():
                    d2h=stats["d2h_bytes"])
 
     # ------------------------------------------------------------- gather --
-    vals = torch.tensor([elapsed, tok, e2e["t"] if e2e else 0.0, e2e["tok"] if e2e else 0.0], dtype=torch.float64,
-                        device=dev)
-    if dist:
-        mx = vals.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = vals.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        elapsed_all, tok_all, e2e_t, e2e_tok = mx[0].item(), sm[1].item(), mx[2].item(), sm[3].item()
-    else:
-        elapsed_all, tok_all, e2e_t, e2e_tok = elapsed, tok, vals[2].item(), vals[3].item()
+    (elapsed_all, e2e_t), (tok_all, e2e_tok) = reduce_counters(
+        [elapsed, e2e["t"] if e2e else 0.0], [tok, e2e["tok"] if e2e else 0.0], device=dev)
     if rank == 0:
         hbm, tf, tf_sus, src = _peaks()
         rows = kt["rows"]
