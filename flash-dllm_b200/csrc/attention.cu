@@ -210,34 +210,41 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         const bool blk = t >= nt_cache;
         const int n0 = blk ? (t - nt_cache) * kKeyTile : c0 + t * kKeyTile;
         const int n_end = blk ? it.blk_rows : c1;
-        // lane covers 16-byte chunk (lane % 16) of keys (lane / 16) + 2i
-#pragma unroll 4
-        for (int i = 0; i < kKeyTile / 2; ++i) {
-          const int key = 2 * i + (lane >> 4);
-          const int chunk = lane & 15;
-          const int n = n0 + key;
-          bool valid = n < n_end;
-          const __nv_bfloat16* ksrc = p.kc;
-          const __nv_bfloat16* vsrc = p.vc;
-          if (valid) {
+        // Resolve the 64 source rows of this tile first (two per lane, one
+        // coalesced load each), so the gathers below issue back to back.
+        int64_t src_row[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int n = n0 + lane + 32 * h;
+          int64_t row = -1;
+          if (n < n_end) {
             if (blk) {
-              const int64_t row = it.blk_q0 + n;
-              ksrc = p.k1 + row * d + head * kHD + chunk * 8;
-              vsrc = p.v1 + row * d + head * kHD + chunk * 8;
+              row = it.blk_q0 + n;
             } else {
               const int64_t pk = static_cast<int64_t>(it.k_base) + n;
-              const int64_t row = (pk < p.n_pos_k) ? p.pos_k[pk] : -1;
+              row = (pk < p.n_pos_k) ? p.pos_k[pk] : -1;
               if (row < 0 || row >= p.n_slots) {
                 report(p.status, FDLLM_ERR_INDEX, static_cast<int>(pk), kAttnKernelId);
-                valid = false;
-              } else {
-                ksrc = p.kc + row * d + head * kHD + chunk * 8;
-                vsrc = p.vc + row * d + head * kHD + chunk * 8;
+                row = -1;
               }
             }
           }
-          cp_async_16_zfill(kt + tile_off(key, chunk), ksrc, valid);
-          cp_async_16_zfill(vt + tile_off(key, chunk), vsrc, valid);
+          src_row[h] = row;
+        }
+        const __nv_bfloat16* kbase_g = blk ? p.k1 : p.kc;
+        const __nv_bfloat16* vbase_g = blk ? p.v1 : p.vc;
+        // lane covers 16-byte chunk (lane % 16) of keys 2i + lane / 16
+#pragma unroll 8
+        for (int i = 0; i < kKeyTile / 2; ++i) {
+          const int key = 2 * i + (lane >> 4);
+          const int chunk = lane & 15;
+          const int64_t r0 = __shfl_sync(0xffffffffu, src_row[0], key & 31);
+          const int64_t r1 = __shfl_sync(0xffffffffu, src_row[1], key & 31);
+          const int64_t row = key < 32 ? r0 : r1;
+          const bool valid = row >= 0;
+          const int64_t off = valid ? row * d + head * kHD + chunk * 8 : 0;
+          cp_async_16_zfill(kt + tile_off(key, chunk), kbase_g + off, valid);
+          cp_async_16_zfill(vt + tile_off(key, chunk), vbase_g + off, valid);
         }
         cp_async_mbar_arrive(&full[s]);
       }

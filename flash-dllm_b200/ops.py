@@ -62,10 +62,14 @@ def _sm_count(index: int) -> int:
 
 
 def auto_kv_splits(items: int, n_heads: int, max_keys: int, device: torch.device) -> int:
-    """Split each key range so the grid covers about two CTAs per SM, keeping
-    at least 128 keys per split."""
+    """Split each key range only when the (item, head) grid leaves SMs idle:
+    then aim at about two CTAs per SM, keeping at least 128 keys per split
+    (a split costs a combine pass)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    target = 2 * _sm_count(idx)
+    sms = _sm_count(idx)
+    if items * n_heads >= sms:
+        return 1
+    target = 2 * sms
     s = max(1, -(-target // max(1, items * n_heads)))
     s = min(s, max(1, max_keys // 128), 16)
     return s
