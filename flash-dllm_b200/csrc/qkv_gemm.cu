@@ -30,10 +30,14 @@ constexpr int kQkvThreads = 192;
 constexpr int kQkvKernelId = 1;
 constexpr int kQkvRingBytes = 192 * 1024;
 
-template <int BN, int XROWS>
+// A ring slot holds KSUB 64-wide K sub-tiles of X and W (one 128-byte swizzle
+// box per operand row each), i.e. 128 * KSUB contiguous bytes of every row.
+template <int BN, int XROWS, int KSUB>
 struct QkvCfg {
-  static constexpr int kABytes = XROWS * kQkvBK * 2;  // MMA reads 128 rows; rows >= XROWS are unused
-  static constexpr int kBBytes = BN * kQkvBK * 2;
+  static constexpr int kASub = XROWS * kQkvBK * 2;  // MMA reads 128 rows; rows >= XROWS are unused
+  static constexpr int kBSub = BN * kQkvBK * 2;
+  static constexpr int kABytes = KSUB * kASub;
+  static constexpr int kBBytes = KSUB * kBSub;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = kQkvRingBytes / kStageBytes;
   static constexpr int kBarOffset = kStages * kStageBytes;
@@ -60,6 +64,7 @@ struct QkvParams {
   int32_t kb_per_split;
   int32_t m_tiles;
   int32_t n_units;
+  int32_t ksub;
 };
 
 struct QkvUnit {
@@ -72,18 +77,18 @@ __device__ __forceinline__ QkvUnit qkv_unit(const QkvParams& p, int u) {
   w.split = u % p.splits;
   w.m_tile = tile % p.m_tiles;
   w.n_tile = tile / p.m_tiles;
-  const int kb_total = p.d_model / kQkvBK;
+  const int kb_total = p.d_model / (kQkvBK * p.ksub);
   w.kb0 = w.split * p.kb_per_split;
   w.nkb = min(kb_total, w.kb0 + p.kb_per_split) - w.kb0;
   return w;
 }
 
-template <int BN, int XROWS>
+template <int BN, int XROWS, int KSUB>
 __global__ void __launch_bounds__(kQkvThreads, 1)
     qkv_rope_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_wq,
                     const __grid_constant__ CUtensorMap map_wk, const __grid_constant__ CUtensorMap map_wv,
                     const QkvParams p) {
-  using C = QkvCfg<BN, XROWS>;
+  using C = QkvCfg<BN, XROWS, KSUB>;
   constexpr int kPerHead = 128 / BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -141,16 +146,21 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
             ok = false;
             break;
           }
-          uint8_t* a = smem + s * C::kStageBytes;
-          uint8_t* b = a + C::kABytes;
-          const int kx = (w.kb0 + i) * kQkvBK;
+          uint8_t* a0 = smem + s * C::kStageBytes;
+          uint8_t* b0 = a0 + C::kABytes;
           mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-          tma_load_2d(a, &map_x, kx, w.m_tile * kQkvBM, &full[s]);
-          if (BN == 128) {
-            tma_load_2d(b, map_w, kx, head * 128, &full[s]);
-          } else {
-            tma_load_2d(b, map_w, kx, head * 128 + pair * (BN / 2), &full[s]);
-            tma_load_2d(b + (BN / 2) * 128, map_w, kx, head * 128 + 64 + pair * (BN / 2), &full[s]);
+#pragma unroll
+          for (int sub = 0; sub < KSUB; ++sub) {
+            uint8_t* a = a0 + sub * C::kASub;
+            uint8_t* b = b0 + sub * C::kBSub;
+            const int kx = ((w.kb0 + i) * KSUB + sub) * kQkvBK;
+            tma_load_2d(a, &map_x, kx, w.m_tile * kQkvBM, &full[s]);
+            if (BN == 128) {
+              tma_load_2d(b, map_w, kx, head * 128, &full[s]);
+            } else {
+              tma_load_2d(b, map_w, kx, head * 128 + pair * (BN / 2), &full[s]);
+              tma_load_2d(b + (BN / 2) * 128, map_w, kx, head * 128 + 64 + pair * (BN / 2), &full[s]);
+            }
           }
         }
       }
@@ -176,12 +186,15 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint8_t* a = smem + s * C::kStageBytes;
-          const uint64_t da = umma_desc_kmajor_sw128(smem_u32(a));
-          const uint64_t db = umma_desc_kmajor_sw128(smem_u32(a + C::kABytes));
+          const uint8_t* a0 = smem + s * C::kStageBytes;
 #pragma unroll
-          for (int k = 0; k < kQkvBK / 16; ++k)
-            umma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+          for (int sub = 0; sub < KSUB; ++sub) {
+            const uint64_t da = umma_desc_kmajor_sw128(smem_u32(a0 + sub * C::kASub));
+            const uint64_t db = umma_desc_kmajor_sw128(smem_u32(a0 + C::kABytes + sub * C::kBSub));
+#pragma unroll
+            for (int k = 0; k < kQkvBK / 16; ++k)
+              umma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || sub > 0 || k > 0) ? 1u : 0u);
+          }
           umma_commit(&empty[s]);
         }
         if (ok) umma_commit(&acc_full[acc]);
@@ -337,6 +350,7 @@ namespace {
 struct QkvPlan {
   int bn;
   int xrows;
+  int ksub;
   int splits;
   int kb_per_split;
   int m_tiles;
@@ -351,12 +365,16 @@ struct QkvPlan {
 // k-blocks per split.
 QkvPlan plan_qkv(int32_t n_rows, int32_t d_model, int32_t n_heads) {
   QkvPlan pl{};
-  const int kb_total = d_model / kQkvBK;
+  int ksub = env_int("FDLLM_QKV_KSUB", 0);
+  if (ksub != 1 && ksub != 2) ksub = 2;
+  if (d_model % (kQkvBK * ksub) != 0) ksub = 1;
+  pl.ksub = ksub;
+  const int kb_total = d_model / (kQkvBK * ksub);
   const int sms = sm_count();
   pl.m_tiles = (n_rows + kQkvBM - 1) / kQkvBM;
   pl.xrows = n_rows <= 64 ? 64 : 128;
   int bn = env_int("FDLLM_QKV_BN", 0);
-  if (bn != 64 && bn != 128) bn = 128;
+  if (bn != 64 && bn != 128) bn = n_rows <= 64 ? 64 : 128;  // measured best at 64 / 512 rows
   pl.bn = bn;
   pl.n_tiles = 3 * n_heads * (128 / bn);
   const int tiles = pl.m_tiles * pl.n_tiles;
@@ -365,7 +383,7 @@ QkvPlan plan_qkv(int32_t n_rows, int32_t d_model, int32_t n_heads) {
     splits = 1;
     if (tiles < sms) {
       double best = 0.0;
-      for (int s = 1; s <= 16 && kb_total / s >= 8; ++s) {
+      for (int s = 1; s <= 16 && kb_total / s >= 8 / ksub; ++s) {
         const int units = tiles * s;
         const int waves = (units + sms - 1) / sms;
         const double bal = static_cast<double>(units) / (static_cast<double>(waves) * sms);
@@ -396,20 +414,20 @@ size_t qkv_ws_bytes(const QkvPlan& pl) {
   return kQkvCounterBytes + tiles * pl.splits * kQkvBM * pl.bn * sizeof(float);
 }
 
-template <int BN, int XROWS>
+template <int BN, int XROWS, int KSUB>
 int launch_qkv_cfg(const CUtensorMap& mx, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                    const QkvParams& p, const QkvPlan& pl, cudaStream_t stream) {
-  using C = QkvCfg<BN, XROWS>;
+  using C = QkvCfg<BN, XROWS, KSUB>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(qkv_rope_kernel<BN, XROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+    if (cudaFuncSetAttribute(qkv_rope_kernel<BN, XROWS, KSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
         cudaSuccess)
       return FDLLM_ERR_CUDA;
     attr_set[dev] = true;
   }
-  qkv_rope_kernel<BN, XROWS><<<pl.grid, kQkvThreads, C::kSmem, stream>>>(mx, mq, mk, mv, p);
+  qkv_rope_kernel<BN, XROWS, KSUB><<<pl.grid, kQkvThreads, C::kSmem, stream>>>(mx, mq, mk, mv, p);
   return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
 }
 
@@ -448,16 +466,24 @@ int launch_qkv(const void* xn, const void* wq, const void* wk, const void* wv, c
   p.kb_per_split = pl.kb_per_split;
   p.m_tiles = pl.m_tiles;
   p.n_units = pl.n_units;
+  p.ksub = pl.ksub;
   if (pl.splits > 1) {
     if (static_cast<size_t>(pl.m_tiles) * pl.n_tiles * sizeof(int32_t) > kQkvCounterBytes) return FDLLM_ERR_ARG;
     p.counters = static_cast<int32_t*>(workspace);
     p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kQkvCounterBytes);
   }
+  if (pl.ksub == 2) {
+    if (pl.bn == 128)
+      return pl.xrows == 64 ? launch_qkv_cfg<128, 64, 2>(mx, mq, mk, mv, p, pl, stream)
+                            : launch_qkv_cfg<128, 128, 2>(mx, mq, mk, mv, p, pl, stream);
+    return pl.xrows == 64 ? launch_qkv_cfg<64, 64, 2>(mx, mq, mk, mv, p, pl, stream)
+                          : launch_qkv_cfg<64, 128, 2>(mx, mq, mk, mv, p, pl, stream);
+  }
   if (pl.bn == 128)
-    return pl.xrows == 64 ? launch_qkv_cfg<128, 64>(mx, mq, mk, mv, p, pl, stream)
-                          : launch_qkv_cfg<128, 128>(mx, mq, mk, mv, p, pl, stream);
-  return pl.xrows == 64 ? launch_qkv_cfg<64, 64>(mx, mq, mk, mv, p, pl, stream)
-                        : launch_qkv_cfg<64, 128>(mx, mq, mk, mv, p, pl, stream);
+    return pl.xrows == 64 ? launch_qkv_cfg<128, 64, 1>(mx, mq, mk, mv, p, pl, stream)
+                          : launch_qkv_cfg<128, 128, 1>(mx, mq, mk, mv, p, pl, stream);
+  return pl.xrows == 64 ? launch_qkv_cfg<64, 64, 1>(mx, mq, mk, mv, p, pl, stream)
+                        : launch_qkv_cfg<64, 128, 1>(mx, mq, mk, mv, p, pl, stream);
 }
 
 }  // namespace
