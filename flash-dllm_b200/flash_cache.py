@@ -87,7 +87,7 @@ def flash_fused_elastic_cache(self, x: torch.Tensor, block_idx, positions, lengt
                                    max_length, x.device)
             scores = attn_scores if block_idx > 1 else None
             ops.attn_cache(q, att, self.k_cache, self.v_cache, plan, cap, scores, 1.0 / (block_m * n_heads),
-                           n_heads, max_length, softmax_scale)
+                           n_heads, max_length, softmax_scale, items_hint=-(-n_rows // 64))
 
     att = self.attn_out(att)
     x = x + self.dropout(att)

@@ -54,6 +54,41 @@ def _tiles(rows: List, j: int, k_end: int, start: int, n: int, bm: int) -> None:
         rows.append((j, k_end, s, min(s + bm, start + n)))
 
 
+class _Forwarder:
+    """Runs the model's forward passes.  A forward whose input shapes were
+    seen before is captured into a CUDA graph (on its second occurrence, after
+    an eager run of that same step sized the workspaces) and replayed from
+    then on, with the step's inputs copied into the graph's static tensors.
+    Forwards are pure functions of their inputs apart from the in-place cache
+    and score updates, which the graph performs exactly like the eager call."""
+
+    def __init__(self, enabled: bool):
+        self.enabled = enabled
+        self.seen = {}
+        self.graphs = {}
+
+    def __call__(self, key, inputs: dict, build):
+        if not self.enabled:
+            return build(inputs)
+        hit = self.graphs.get(key)
+        if hit is not None:
+            static, graph, out = hit
+            for name, t in inputs.items():
+                static[name].copy_(t)
+            graph.replay()
+            return out
+        self.seen[key] = self.seen.get(key, 0) + 1
+        if self.seen[key] < 2:
+            return build(inputs)
+        static = {name: t.clone() for name, t in inputs.items()}
+        result = build(static)  # this step's real forward; also sizes workspaces
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = build(static)
+        self.graphs[key] = (static, graph, out)
+        return result
+
+
 class _Slots:
     """Host-side state of the sequence slots (the reference's per-slot lists)."""
 
@@ -73,14 +108,15 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                              mask_id=126336, threshold=0.9, gamma=0.9, track_num=4, mask_num=4, eos_id=126081,
                              verify=False, sliding_window=True, is_instruct=True, tokenizer=None, stop_tokens=None,
                              min_keep: int = 1, trace: Optional[list] = None, max_steps: Optional[int] = None,
-                             step_hook=None, record=None, stats: Optional[dict] = None):
+                             step_hook=None, record=None, stats: Optional[dict] = None, use_graphs: bool = True):
     """Returns ``(responses, num_tokens, max_num_tokens)`` like the reference;
     ``responses[i]`` is the decoded text (token ids when ``tokenizer`` is
     None) and ``n_steps[i]`` counts the steps of prompt ``i``.  ``max_steps``
     stops early (benchmarking); ``step_hook(step)`` runs after each step;
     ``record(verify, x_query, query_pos, key_pos, logits, logit_rows,
     attn_scores)`` sees every forward (tests replay it through the oracle);
-    ``stats`` (a dict) accumulates ``h2d_bytes`` / ``d2h_bytes`` / ``steps``."""
+    ``stats`` (a dict) accumulates ``h2d_bytes`` / ``d2h_bytes`` / ``steps``;
+    ``use_graphs`` replays repeated forward shapes as CUDA graphs."""
     dev = model.device
     cfg = model.config
     io = stats if stats is not None else {}
@@ -117,6 +153,7 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
     masks = [torch.from_numpy(_verify_mask(bm, s)).to(dev) for s in range(bm // 2 + 1)]
     ar_L = torch.arange(L, device=dev)
     st = _Slots(B)
+    forward = _Forwarder(use_graphs and dev.type == "cuda")
     count = 0
     start_layer = [-1] * B
 
@@ -164,15 +201,21 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                 _tiles(t_rows, j, st.seqlen_k[j], acc, n, bm)
                 acc += n
         tables = h2d(torch.tensor(m_rows + t_rows, dtype=torch.int64).reshape(-1, 4))
-        masked_blocks = tables[:len(m_rows)] if m_rows else empty_i32
-        tracked_blocks = tables[len(m_rows):] if t_rows else empty_i32
         query_pos_flat = torch.cat([st.masked[j] for j in act] + [st.tracked[j] for j in act])
         x_query = x[query_pos_flat]
-        positions = [query_pos_flat, empty_i64, rotary_emb_pos, [], attn_scores, []]
-        lengths = [start_layer, None, masked_blocks, tracked_blocks, tables, st.active, len(m_rows), L, bm, bn,
-                   None, False]
-        logits = model(x_query.unsqueeze(0), use_cache=True, lengths=lengths, positions=positions,
-                       logit_rows=r_m).logits[0]
+        n_m = len(m_rows)
+
+        def cache_forward(t, n_m=n_m, r_m=r_m, has_t=bool(t_rows)):
+            masked_blocks = t["tables"][:n_m] if n_m else empty_i32
+            tracked_blocks = t["tables"][n_m:] if has_t else empty_i32
+            positions = [t["qpos"], empty_i64, rotary_emb_pos, [], attn_scores, []]
+            lengths = [start_layer, None, masked_blocks, tracked_blocks, t["tables"], st.active, n_m, L, bm, bn,
+                       None, False]
+            return model(t["x"].unsqueeze(0), use_cache=True, lengths=lengths, positions=positions,
+                         logit_rows=r_m).logits[0]
+
+        logits = forward(("cache", x_query.numel(), n_m, len(t_rows), r_m),
+                         {"x": x_query, "qpos": query_pos_flat, "tables": tables}, cache_forward)
         if record is not None:
             record(False, x_query, query_pos_flat, None, logits, torch.arange(r_m, device=dev), attn_scores)
         p_max, x0, _ = ops.row_stats(logits)
@@ -223,13 +266,18 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
             attn_mask = torch.cat([masks[s] for s in s_list])
             vblocks = h2d(torch.tensor(vrows, dtype=torch.int32))
             lidx = h2d(torch.tensor(logit_idx, dtype=torch.int64))
-            positions = [qpos, key_pos_flat, rotary_emb_pos, [], attn_scores, attn_mask]
-            lengths = [start_layer, vblocks, None, tracked_blocks, None, st.active, len(m_rows), L, bm, bn, None,
-                       True]
             draft_slots = torch.cat(draft_parts) if draft_parts else empty_i64
+
+            def verify_forward(t, n_m=n_m):
+                positions = [t["qpos"], t["kpos"], rotary_emb_pos, [], attn_scores, t["mask"]]
+                lengths = [start_layer, t["vblocks"], None, empty_i32, None, st.active, n_m, L, bm, bn, None, True]
+                return model(t["x"].unsqueeze(0), use_cache=True, lengths=lengths, positions=positions,
+                             logit_rows=t["lidx"]).logits[0]
+
             if sum(s_list) > 0:
-                logits_v = model(x_verify.unsqueeze(0), use_cache=True, lengths=lengths, positions=positions,
-                                 logit_rows=lidx).logits[0]
+                logits_v = forward(("verify", x_verify.numel(), key_pos_flat.numel(), len(vrows), lidx.numel()),
+                                   {"x": x_verify, "qpos": qpos, "kpos": key_pos_flat, "mask": attn_mask,
+                                    "vblocks": vblocks, "lidx": lidx}, verify_forward)
                 if record is not None:
                     record(True, x_verify, qpos, key_pos_flat, logits_v, lidx, attn_scores)
                 draft_tok = x_draft[draft_slots]

@@ -20,18 +20,25 @@ BF16 = torch.bfloat16
 
 
 class Workspace:
-    """Grow-only zero-initialised device scratch, one per (device, tag)."""
+    """Grow-only zero-initialised device scratch, one per (device, tag).
+
+    Buffers that were outgrown stay allocated (in ``_retired``): a captured
+    CUDA graph may still hold their addresses."""
 
     _bufs: Dict[Tuple[int, str], torch.Tensor] = {}
+    _retired: list = []
 
     @classmethod
     def get(cls, device: torch.device, nbytes: int, tag: str = "main") -> torch.Tensor:
         key = (device.index if device.index is not None else torch.cuda.current_device(), tag)
         buf = cls._bufs.get(key)
         if buf is None or buf.numel() < nbytes:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("workspace must be sized by an eager call before graph capture")
             size = max(nbytes, 1 << 20)
             if buf is not None:
                 size = max(size, int(buf.numel() * 1.5))
+                cls._retired.append(buf)
             buf = torch.zeros(size, dtype=torch.uint8, device=device)
             cls._bufs[key] = buf
         return buf
@@ -39,6 +46,7 @@ class Workspace:
     @classmethod
     def clear(cls) -> None:
         cls._bufs.clear()
+        cls._retired.clear()
 
 
 def _check(t: torch.Tensor, name: str, dtype=None, dim=None) -> None:
@@ -136,15 +144,18 @@ def plan_cache_attention(masked_blocks, tracked_blocks, n_rows: int, batch_size:
 
 
 def attn_cache(q, o, k_cache, v_cache, plan: torch.Tensor, capacity: int, attn_scores, score_scale: float,
-               n_heads: int, seqlen_max: int, softmax_scale: float, kv_splits: int = 0) -> None:
-    """Masked + tracked attention over the cache, optional fused score accumulation."""
+               n_heads: int, seqlen_max: int, softmax_scale: float, kv_splits: int = 0,
+               items_hint: int = 0) -> None:
+    """Masked + tracked attention over the cache, optional fused score
+    accumulation.  ``items_hint`` estimates the plan's real item count (the
+    capacity is an upper bound) for the automatic key split."""
     for t, n in ((q, "q"), (o, "o"), (k_cache, "k_cache"), (v_cache, "v_cache")):
         _check(t, n, BF16, 2)
     if attn_scores is not None:
         _check(attn_scores, "attn_scores", torch.float32)
     d_model = q.shape[1]
     if kv_splits <= 0:
-        kv_splits = auto_kv_splits(capacity, n_heads, seqlen_max, q.device)
+        kv_splits = auto_kv_splits(items_hint if items_hint > 0 else capacity, n_heads, seqlen_max, q.device)
     nbytes = _lib.lib().fdllm_attn_workspace_bytes(capacity, n_heads, kv_splits)
     ws = Workspace.get(q.device, nbytes, "attn")
     call("fdllm_attn_cache", ptr(q), ptr(o), ptr(k_cache), ptr(v_cache), ptr(plan), capacity, ptr(attn_scores),
