@@ -415,12 +415,15 @@ def run_kernels_only(seqs: int) -> None:
 
 
 def _count_launches(model, per, args):
-    """Kernels of this library launched per decode step: per layer RMSNorm x2,
-    QKV, plan (first layer of the cache forward), attention (+ combine when
-    split) in the cache forward and QKV + attention in the verify forward, plus
-    row_stats x2, window_accept, verify_accept, refresh_sort per step."""
+    """Kernels of this library launched per decode step.  Each forward (the
+    cache forward and the verify forward) launches per layer RMSNorm, the QKV
+    GEMM, attention, the fused residual-add + RMSNorm and SwiGLU, plus ln_f's
+    RMSNorm; the cache forward adds the attention plan.  The step's decisions
+    add row_stats x2, window_accept, verify_accept and refresh_sort.  Split-KV
+    combine launches (only when the grid underfills) are not counted."""
     n_layers = model.config.n_layers
-    return n_layers * (2 + 1 + 1) + 1 + n_layers * (2 + 1 + 1) + 5
+    per_forward = n_layers * 5 + 1
+    return 2 * per_forward + 1 + 5
 
 
 if __name__ == "__main__":

@@ -14,9 +14,11 @@ The attention half runs on this package's sm_100a kernels: RMSNorm, the
 tcgen05 QKV + RoPE + cache-scatter GEMM (or its verify variant), and one
 fused masked + tracked attention pass (or the verify attention).  The
 reference's ``S`` tensor and ``attn_scores += S.mean((0, 1))`` become an
-in-kernel accumulation.  The projections after attention (``attn_out`` and
-the SwiGLU MLP) are the block's own ``nn.Linear`` modules, as in the
-reference.
+in-kernel accumulation.  After attention, the residual add and ``ff_norm``
+run as one kernel and so do SiLU and the gate product; the projections
+(``attn_out``, ``ff_proj``/``up_proj`` -- one GEMM when the model stacked
+their weights as ``ffup_weight`` -- and ``ff_out``) are the block's own
+weights through cuBLAS, as in the reference.
 """
 from __future__ import annotations
 
@@ -27,11 +29,15 @@ import torch
 from . import ops
 
 
-def _norm(module, x: torch.Tensor) -> torch.Tensor:
+def _norm_weight(module) -> torch.Tensor:
     w = getattr(module, "weight", None)
     if w is None or w.dtype != torch.bfloat16 or getattr(module, "bias", None) is not None:
         raise TypeError("flash_fused_elastic_cache needs bf16 RMSNorm modules with a weight and no bias")
-    return ops.rmsnorm(x, w, float(getattr(module, "eps", 1e-5)))
+    return w
+
+
+def _eps(module) -> float:
+    return float(getattr(module, "eps", 1e-5))
 
 
 class _PlanCache:
@@ -67,7 +73,7 @@ def flash_fused_elastic_cache(self, x: torch.Tensor, block_idx, positions, lengt
     softmax_scale = softmax_scale or (1.0 / math.sqrt(head_dim))
     x = x.contiguous()
     n_rows = x.shape[0]
-    x_normed = _norm(self.attn_norm, x)
+    x_normed = ops.rmsnorm(x, _norm_weight(self.attn_norm), _eps(self.attn_norm))
     att = torch.empty_like(x)
     q = torch.empty_like(x)
     sin, cos = rotary_emb_pos
@@ -90,11 +96,19 @@ def flash_fused_elastic_cache(self, x: torch.Tensor, block_idx, positions, lengt
                            n_heads, max_length, softmax_scale, items_hint=-(-n_rows // 64))
 
     att = self.attn_out(att)
-    x = x + self.dropout(att)
-    og_x = x
-    h = _norm(self.ff_norm, x)
-    h, h_up = self.ff_proj(h), self.up_proj(h)
-    h = self.act(h) * h_up
+    # x + att and ff_norm(x + att) in one kernel (dropout is p=0 at inference)
+    og_x, h = ops.add_rmsnorm(x, att, _norm_weight(self.ff_norm), _eps(self.ff_norm))
+    fused = getattr(self, "ffup_weight", None)
+    if fused is not None:  # [ff_proj; up_proj] stacked: one GEMM
+        gu = torch.nn.functional.linear(h, fused)
+        hid = gu.shape[1] // 2
+        gate, up = gu[:, :hid], gu[:, hid:]
+    else:
+        gate, up = self.ff_proj(h), self.up_proj(h)
+    if isinstance(self.act, torch.nn.SiLU):
+        h = ops.swiglu(gate, up)
+    else:
+        h = self.act(gate) * up
     h = self.ff_out(h)
     h = self.dropout(h)
     return (og_x + h).unsqueeze(0)

@@ -73,6 +73,19 @@ class LLaDABlockB200(nn.Module):
     def forward(self, x, positions=None, lengths=None, block_idx=0):
         return flash_fused_elastic_cache(self, x.squeeze(0), block_idx, positions, lengths)
 
+    @torch.no_grad()
+    def fuse_mlp_weights(self) -> None:
+        """Stack ``ff_proj`` and ``up_proj`` weights into one (2*hidden,
+        d_model) tensor ``ffup_weight`` so the operator runs one GEMM for
+        both; the two Linear weights become views of it (no extra memory, and
+        a later ``load_state_dict`` copies into the views)."""
+        w1, w2 = self.ff_proj.weight, self.up_proj.weight
+        fused = torch.cat([w1.detach(), w2.detach()], 0)
+        h = w1.shape[0]
+        self.ff_proj.weight = nn.Parameter(fused[:h], requires_grad=False)
+        self.up_proj.weight = nn.Parameter(fused[h:], requires_grad=False)
+        self.ffup_weight = fused
+
 
 class _Transformer(nn.Module):
     def __init__(self, cfg, device, dtype):
@@ -116,7 +129,13 @@ class LLaDAModelB200(nn.Module):
                     p.fill_(1.0)
                 else:
                     p.normal_(0.0, std, generator=g)
+        m.fuse_mlp_weights()
         return m.eval()
+
+    def fuse_mlp_weights(self) -> None:
+        """``LLaDABlockB200.fuse_mlp_weights`` on every block."""
+        for blk in self.model.transformer.blocks:
+            blk.fuse_mlp_weights()
 
     @torch.no_grad()
     def forward(self, input_ids: torch.Tensor, use_cache: bool = True, lengths=None, positions=None,

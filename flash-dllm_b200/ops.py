@@ -91,6 +91,35 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[tor
     return y
 
 
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float):
+    """(y, h) = (x + residual, RMSNorm(x + residual)) in one pass."""
+    _check(x, "x", BF16, 2)
+    _check(residual, "residual", BF16, 2)
+    _check(weight, "weight", BF16, 1)
+    y = torch.empty_like(x)
+    h = torch.empty_like(x)
+    call("fdllm_add_rmsnorm", ptr(x), ptr(residual), ptr(weight), ptr(y), ptr(h), x.shape[0], x.shape[1],
+         float(eps), _stream())
+    return y, h
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """bf16(silu(gate)) * up for [rows, cols] tensors; gate/up may be the
+    column halves of one stacked GEMM output (same row stride, unit column
+    stride), read in place."""
+    if gate.shape != up.shape or gate.dim() != 2:
+        raise ValueError("gate and up must be 2-D of the same shape")
+    for t, name in ((gate, "gate"), (up, "up")):
+        if t.dtype != BF16 or not t.is_cuda or t.stride(1) != 1:
+            raise ValueError(f"{name} must be a CUDA bf16 tensor with unit column stride")
+    if gate.stride(0) != up.stride(0):
+        raise ValueError("gate and up must share a row stride")
+    out = torch.empty(gate.shape, dtype=BF16, device=gate.device)
+    call("fdllm_swiglu", ptr(gate), ptr(up), ptr(out), gate.shape[0], gate.shape[1],
+         gate.stride(0) if gate.shape[0] > 1 else gate.shape[1], _stream())
+    return out
+
+
 def _qkv(entry: str, xn, wq, wk, wv, pos, sin, cos, q_out, k_out, v_out, n_heads: int) -> None:
     for t, n in ((xn, "xn"), (wq, "wq"), (wk, "wk"), (wv, "wv"), (q_out, "q_out"), (k_out, "k_out"),
                  (v_out, "v_out")):

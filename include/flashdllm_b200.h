@@ -57,6 +57,19 @@ int fdllm_status_read(int32_t out[4], cudaStream_t stream);
 int fdllm_rmsnorm(const void* x, const void* weight, void* y, int32_t rows, int32_t dim, float eps,
                   cudaStream_t stream);
 
+/* Residual add fused with the next RMSNorm: y = bf16(x + residual), h = RMSNorm(y) with the rounding
+ * points of fdllm_rmsnorm; x, residual, y, h bf16 [rows, dim] (dim <= 4096).
+ * ref llada/flash_cache_triton.py:618-627 (x + dropout(att); ff_norm(x)). */
+int fdllm_add_rmsnorm(const void* x, const void* residual, const void* weight, void* y, void* h, int32_t rows,
+                      int32_t dim, float eps, cudaStream_t stream);
+
+/* SwiGLU product out = bf16(silu(gate)) * up (silu in fp32): gate and up are [rows, cols] bf16 with row
+ * stride ld_in elements (e.g. the two column halves of one [rows, 2*cols] GEMM output), out is contiguous
+ * [rows, cols]; cols and ld_in multiples of 8.
+ * ref llada/flash_cache_triton.py:628-633 (act(ff_proj(x)) * up_proj(x)). */
+int fdllm_swiglu(const void* gate, const void* up, void* out, int64_t rows, int32_t cols, int64_t ld_in,
+                 cudaStream_t stream);
+
 /* Workspace (bytes) fdllm_qkv_rope_cache / fdllm_verify_qkv need for n_rows query rows. */
 size_t fdllm_qkv_workspace_bytes(int32_t n_rows, int32_t d_model, int32_t n_heads);
 

@@ -28,6 +28,7 @@ def _model():
                         eos_token_id=cases.GEN_KW["eos_id"])
     m = LLaDAModelB200(c, device="cuda")
     m.load_state_dict({k: v.to(torch.bfloat16) for k, v in w.items()}, strict=True)
+    m.fuse_mlp_weights()
     return m.eval()
 
 

@@ -32,10 +32,13 @@ def _blocks(d_model=1024, n_heads=8, hidden=2048):
     return cpu, gpu
 
 
-def test_layer_flash_cache_mode():
+@pytest.mark.parametrize("fused_mlp", [False, True])
+def test_layer_flash_cache_mode(fused_mlp):
     from flash_dllm_b200.flash_cache import flash_fused_elastic_cache
     d, H, bm, L, B = 1024, 8, 32, 384, 3
     cpu, gpu = _blocks(d, H)
+    if fused_mlp:
+        gpu.fuse_mlp_weights()
     g = torch.Generator().manual_seed(1)
     masked_counts, tracked_counts, seqlen_k = [32, 32, 32], [64, 5, 0], [384, 256, 128]
     mb, tb = do.build_block_tables(masked_counts, tracked_counts, seqlen_k, bm)
@@ -100,3 +103,30 @@ def test_layer_flash_verify_mode():
     y = flash_fused_elastic_cache(gpu, x.cuda(), 3, positions, lengths).squeeze(0)
     assert _rel(y, y_ref) <= TOL
     assert torch.equal(gpu.k_cache.cpu(), kc)  # verify never writes the cache
+
+
+def test_add_rmsnorm_and_swiglu():
+    from flash_dllm_b200 import ops
+    g = torch.Generator().manual_seed(7)
+    for rows, dim in [(1, 8), (5, 1024), (37, 4096), (130, 2048)]:
+        x = torch.randn(rows, dim, generator=g).bfloat16()
+        r = torch.randn(rows, dim, generator=g).bfloat16()
+        w = (1 + 0.1 * torch.randn(dim, generator=g)).bfloat16()
+        y, h = ops.add_rmsnorm(x.cuda(), r.cuda(), w.cuda(), 1e-5)
+        y_ref = x + r
+        assert torch.equal(y.cpu(), y_ref)  # one bf16 rounding, same as torch
+        assert _rel(h, fco.rms_norm(y_ref, w, 1e-5)) <= 1e-2
+    y, h = ops.add_rmsnorm(x[:0].cuda(), r[:0].cuda(), w.cuda(), 1e-5)
+    assert y.shape == (0, 2048) and h.shape == (0, 2048)
+    for n in [8, 4096, 3 * 12288]:
+        a = (3 * torch.randn(n // 8, 8, generator=g)).bfloat16()
+        b = torch.randn(n // 8, 8, generator=g).bfloat16()
+        out = ops.swiglu(a.cuda(), b.cuda()).cpu()
+        ref = torch.nn.functional.silu(a.float()).bfloat16() * b
+        # silu may differ by one bf16 ulp where exp rounds differently
+        assert (out.float() - ref.float()).abs().max() <= 2 ** -7 * ref.float().abs().max()
+    # column halves of one stacked tensor (the fused MLP GEMM output)
+    gu = torch.randn(9, 2 * 256, generator=g).bfloat16().cuda()
+    out = ops.swiglu(gu[:, :256], gu[:, 256:])
+    ref = torch.nn.functional.silu(gu[:, :256].float()).bfloat16() * gu[:, 256:]
+    assert _rel(out, ref) <= 1e-2
