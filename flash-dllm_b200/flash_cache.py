@@ -14,11 +14,11 @@ The attention half runs on this package's sm_100a kernels: RMSNorm, the
 tcgen05 QKV + RoPE + cache-scatter GEMM (or its verify variant), and one
 fused masked + tracked attention pass (or the verify attention).  The
 reference's ``S`` tensor and ``attn_scores += S.mean((0, 1))`` become an
-in-kernel accumulation.  After attention, the residual add and ``ff_norm``
-run as one kernel and so do SiLU and the gate product; the projections
-(``attn_out``, ``ff_proj``/``up_proj`` -- one GEMM when the model stacked
-their weights as ``ffup_weight`` -- and ``ff_out``) are the block's own
-weights through cuBLAS, as in the reference.
+in-kernel accumulation.  After attention, the projections (``attn_out``,
+``ff_proj``/``up_proj`` -- one GEMM when the model stacked their weights as
+``ffup_weight`` -- and ``ff_out``) are the block's own weights through
+cuBLAS, as in the reference, with both residual adds in the GEMM epilogues
+(``addmm``) and SiLU times the gate in one kernel.
 """
 from __future__ import annotations
 
@@ -95,9 +95,17 @@ def flash_fused_elastic_cache(self, x: torch.Tensor, block_idx, positions, lengt
             ops.attn_cache(q, att, self.k_cache, self.v_cache, plan, cap, scores, 1.0 / (block_m * n_heads),
                            n_heads, max_length, softmax_scale, items_hint=-(-n_rows // 64))
 
-    att = self.attn_out(att)
-    # x + att and ff_norm(x + att) in one kernel (dropout is p=0 at inference)
-    og_x, h = ops.add_rmsnorm(x, att, _norm_weight(self.ff_norm), _eps(self.ff_norm))
+    # Residual adds: into the GEMM epilogue (C = x + att W^T, one bf16 rounding
+    # of the sum instead of two) when the projection is a plain bias-free
+    # Linear and dropout is the identity; else the add is fused with ff_norm.
+    plain = _plain_linear(self.attn_out) and _plain_linear(self.ff_out) and isinstance(
+        self.dropout, torch.nn.Identity)
+    if plain:
+        og_x = torch.addmm(x, att, self.attn_out.weight.t())
+        h = ops.rmsnorm(og_x, _norm_weight(self.ff_norm), _eps(self.ff_norm))
+    else:
+        og_x, h = ops.add_rmsnorm(x, self.dropout(self.attn_out(att)), _norm_weight(self.ff_norm),
+                                  _eps(self.ff_norm))
     fused = getattr(self, "ffup_weight", None)
     if fused is not None:  # [ff_proj; up_proj] stacked: one GEMM
         gu = torch.nn.functional.linear(h, fused)
@@ -109,9 +117,14 @@ def flash_fused_elastic_cache(self, x: torch.Tensor, block_idx, positions, lengt
         h = ops.swiglu(gate, up)
     else:
         h = self.act(gate) * up
-    h = self.ff_out(h)
-    h = self.dropout(h)
+    if plain:
+        return torch.addmm(og_x, h, self.ff_out.weight.t()).unsqueeze(0)
+    h = self.dropout(self.ff_out(h))
     return (og_x + h).unsqueeze(0)
+
+
+def _plain_linear(m) -> bool:
+    return type(m) is torch.nn.Linear and m.bias is None and m.weight.dtype == torch.bfloat16
 
 
 def install_into_reference(modeling_module) -> None:
