@@ -465,6 +465,482 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   }
 }
 
+// ---------------------------------------------------------------------------
+// tcgen05 cache attention.  Same work items, key slicing, split-KV partial
+// format and results as attn_kernel<false>, with the products on the
+// 5th-generation tensor cores: S = Q K^T and O += P V are M=128 UMMAs issued
+// by one thread, S (double-buffered) and the O accumulator live in tensor
+// memory, and only P passes through shared memory (bf16, 128-byte swizzled:
+// the A operand of the second product).  V is read in place as an MN-major B
+// operand.
+//
+// A kernel that uses tensor memory runs one CTA per SM, so each CTA runs two
+// independent pipelines ("halves"), each on its own work item (items 2x and
+// 2x+1 of the grid's x index) with its own shared memory, barriers and 256
+// TMEM columns.  A tcgen05.mma costs about the same issue time for any
+// M <= 128 and N <= 128, so each half issues few, wide ones: per 64-key tile
+// one M=128, N=64 S product (8 K-steps) and one M=128, N=128 PV product
+// (4 K-steps).  The 128 rows of a half's S operand are its 64 query rows and
+// qbar = the fp32 sum of its masked query rows split into bf16 hi + lo, whose
+// S rows are exactly the raw-logit column sums the reference accumulates into
+// attn_scores -- computed by the same instruction.  Half 0 keeps its query
+// rows in rows / TMEM lanes 0-63 and qbar in 64-65; half 1 the other way
+// round (qbar 0-1, query rows 64-127), so the two halves' softmax warps sit in
+// different TMEM lane quarters, i.e. on different SM sub-partitions.  Operand
+// rows that carry nothing are never read back, so their shared-memory windows
+// may overlap other buffers.
+//
+// Warps (12): softmax h0: 0,1 (lanes 0-63)   softmax h1: 2,3 (lanes 64-127)
+//             scores  h1: 4 (lanes 0-31)     scores  h0: 6 (lanes 64-95)
+//             MMA h0: 5, h1: 7     K producer h0: 8, h1: 10     V producer
+//             h0: 9, h1: 11.  Warp 8 owns TMEM (512 columns).
+// Softmax: thread = one query row, all 64 keys of a tile.  The reference max
+// of a row only moves (and O is rescaled in TMEM) when a tile raises the row
+// max by more than 2^8, so P stays within bf16 range and O is rarely touched;
+// l and O always share the reference max.
+// Per 64-key tile t of a half (2 K and 2 V stages, 2 S buffers, 2 P buffers):
+//   producers: K(t) -> k_full, V(t) -> v_full (never waiting on each other)
+//   MMA:       S(t) -> s_full, k_empty;  then PV(t-1) after p_full(t-1) ->
+//              pv_done, v_empty
+//   softmax:   S(t) -> s_empty;  P(t) -> p_full once PV(t-2) freed the buffer
+//   scores:    S(t) rows of qbar -> s_empty, atomics
+// ---------------------------------------------------------------------------
+constexpr int kTcWarps = 12;
+constexpr int kTcThreads = kTcWarps * 32;
+constexpr uint32_t kTcTmemCols = 512;
+constexpr float kTcRescaleThreshold = 8.f;  // log2 units
+constexpr int kTcPBytes = kItemRows * 128;  // 64 rows x 64 keys
+constexpr int kTcWin = 128 * 128;           // bytes an M=128 A operand reads from its base
+// Half 0 (query rows 0-63, qbar rows 64/65): Q halves of 72 rows (9 KB) each
+constexpr int kH0Q0 = 0, kH0Q1 = 9 * 1024, kH0P = 18 * 1024, kH0K = 34 * 1024, kH0V = 66 * 1024,
+              kH0Scr = 98 * 1024, kH0Bar = kH0Scr + 256, kH0End = 99 * 1024;
+// Half 1 (qbar rows 0/1, query rows 64-127): Q windows of 16 KB each, the
+// query rows in their second 8 KB; P buffers are read from 8 KB before them.
+constexpr int kH1Base = kH0End;
+constexpr int kH1Q0 = kH1Base, kH1Q1 = kH1Base + 16 * 1024, kH1P = kH1Base + 32 * 1024,
+              kH1K = kH1Base + 48 * 1024, kH1V = kH1Base + 80 * 1024, kH1Scr = kH1Base + 112 * 1024,
+              kH1Bar = kH1Scr + 256, kH1End = kH1Base + 113 * 1024;
+constexpr int kTcSmem = 1024 + kH1End;
+static_assert(kH0Q0 + kTcWin <= kH0End && kH0Q1 + kTcWin <= kH1End && kH0P + kTcPBytes + kTcWin <= kH1End,
+              "half-0 operand windows inside shared memory");
+static_assert(kH1P - 8 * 1024 >= 0 && kH1P + kTcPBytes + 8 * 1024 <= kH1End && kH1Q1 + kTcWin <= kH1End,
+              "half-1 operand windows inside shared memory");
+static_assert(kTcSmem <= 227 * 1024, "shared memory");
+
+struct TcHalf {
+  uint32_t row_lane;   // TMEM lane / operand row of query row 0
+  uint32_t qbar_lane;  // TMEM lane / operand row of qbar hi
+  uint8_t* q_win0;     // S operand windows (64-dim halves)
+  uint8_t* q_win1;
+  uint8_t* p_row0;     // P buffer 0: address of query row 0's P row (+ b * kTcPBytes)
+  uint8_t* p_win;      // P buffer 0 operand window (+ b * kTcPBytes)
+  uint8_t* k;          // K stage 0 (+ s * kTileBytes)
+  uint8_t* v;          // V stage 0 (+ s * kTileBytes)
+  float* scr;
+  uint64_t* bar;
+  uint32_t col;        // first TMEM column of this half
+};
+
+__device__ __forceinline__ TcHalf tc_half(uint8_t* smem, int h) {
+  TcHalf H;
+  H.row_lane = h ? 64u : 0u;
+  H.qbar_lane = h ? 0u : 64u;
+  H.q_win0 = smem + (h ? kH1Q0 : kH0Q0);
+  H.q_win1 = smem + (h ? kH1Q1 : kH0Q1);
+  H.p_row0 = smem + (h ? kH1P : kH0P);
+  H.p_win = H.p_row0 - (h ? 8 * 1024 : 0);
+  H.k = smem + (h ? kH1K : kH0K);
+  H.v = smem + (h ? kH1V : kH0V);
+  H.scr = reinterpret_cast<float*>(smem + (h ? kH1Scr : kH0Scr));
+  H.bar = reinterpret_cast<uint64_t*>(smem + (h ? kH1Bar : kH0Bar));
+  H.col = h ? 256u : 0u;
+  return H;
+}
+
+// operand row `row` (0..127) of a K-major SW128 window: 16-byte chunk c
+__device__ __forceinline__ uint8_t* win_chunk(uint8_t* win, int row, int c) {
+  return win + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                   const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int split = blockIdx.z;
+
+  // warp -> (half, role): 0,1 softmax h0 | 2,3 softmax h1 | 4 scores h1 |
+  // 5 MMA h0 | 6 scores h0 | 7 MMA h1 | 8 K h0 | 9 V h0 | 10 K h1 | 11 V h1
+  enum Role { kSoftmax, kScores, kMma, kProdK, kProdV };
+  const int role = warp < 4 ? kSoftmax
+                   : warp >= 8 ? ((warp & 1) ? kProdV : kProdK)
+                               : ((warp & 1) ? kMma : kScores);
+  const int h = warp < 4 ? (warp >> 1) : warp >= 8 ? ((warp >> 1) & 1) : (warp == 4 || warp == 7) ? 1 : 0;
+  const TcHalf H = tc_half(smem, h);
+  uint64_t* k_full = H.bar;
+  uint64_t* k_empty = H.bar + 2;
+  uint64_t* v_full = H.bar + 4;
+  uint64_t* v_empty = H.bar + 6;
+  uint64_t* s_full = H.bar + 8;
+  uint64_t* s_empty = H.bar + 10;
+  uint64_t* p_full = H.bar + 12;
+  uint64_t* pv_done = H.bar + 14;
+  uint64_t* mma_done = H.bar + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kH0Bar + 18 * 8);
+  volatile int32_t* fail = reinterpret_cast<volatile int32_t*>(H.bar + 17);
+
+  // this half's work item
+  const int item_id = 2 * blockIdx.x + h;
+  Item it{};
+  const bool has_item = load_item(p, false, item_id, it);
+  int c0 = 0, c1 = 0, n_tiles = 0;
+  if (has_item) {
+    const int per = ((it.n_keys + p.kv_splits - 1) / p.kv_splits + kKeyTile - 1) / kKeyTile * kKeyTile;
+    c0 = min(it.n_keys, split * per);
+    c1 = min(it.n_keys, c0 + per);
+    n_tiles = (c1 - c0 + kKeyTile - 1) / kKeyTile;
+  }
+  const bool scores_on = has_item && p.scores != nullptr && it.m_len > 0;
+  const int64_t d = p.d_model;
+  {
+    // the CTA exits only when neither half has an item
+    Item other{};
+    const bool other_has = load_item(p, false, 2 * blockIdx.x + (1 - h), other);
+    if (!has_item && !other_has) return;  // uniform across the CTA
+  }
+
+  if (role == kMma && lane == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], scores_on ? 3 : 2);
+      mbar_init(&p_full[s], 2);
+      mbar_init(&pv_done[s], 1);
+    }
+    mbar_init(mma_done, 1);
+    *fail = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, kTcTmemCols);
+    if (lane == 0) {
+      tma_prefetch_desc(&map_k);
+      tma_prefetch_desc(&map_v);
+    }
+  }
+  if (warp < 8) {
+    // operand fill of half f by threads [128 f, 128 f + 128): query rows (rows
+    // past the item zero), qbar hi / lo, the other rows of qbar's 8-row atom
+    // zero.  All eight loads of a thread are in flight together.
+    const int f = threadIdx.x >> 7, tid = threadIdx.x & 127;
+    const TcHalf F = tc_half(smem, f);
+    Item fi{};
+    const bool f_has = load_item(p, false, 2 * blockIdx.x + f, fi);
+    constexpr int kPer = kItemRows * 16 / 128;
+    uint4 v[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int row = (tid + 128 * k) >> 4, c = tid & 15;
+      v[k] = (f_has && row < fi.rows)
+                 ? *reinterpret_cast<const uint4*>(p.q + item_row(fi, row) * d + head * kHD + c * 8)
+                 : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int row = (tid + 128 * k) >> 4, c = tid & 15;
+      *reinterpret_cast<uint4*>(win_chunk((c >> 3) ? F.q_win1 : F.q_win0, F.row_lane + row, c)) = v[k];
+    }
+    if (tid < 2 * 8 * 8) {  // qbar's atom: 8 rows x 8 chunks x 2 halves
+      const int hh = tid >> 6, rr = F.qbar_lane + ((tid >> 3) & 7), ch = tid & 7;
+      *reinterpret_cast<uint4*>(win_chunk(hh ? F.q_win1 : F.q_win0, rr, ch)) = make_uint4(0, 0, 0, 0);
+    }
+    const bool f_scores = f_has && p.scores != nullptr && fi.m_len > 0;
+    if (f_scores) {
+      // qbar dim = tid: fp32 sum over the masked rows (the item's first m_len
+      // rows) -> bf16 hi (row qbar_lane) and lo (row qbar_lane + 1)
+      if (f == 0)
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      else
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+      const int dim = tid, c = (dim & 63) >> 3;
+      uint8_t* win = (dim >> 6) ? F.q_win1 : F.q_win0;
+      float acc = 0.f;
+      for (int r = 0; r < fi.m_len; ++r)
+        acc += __bfloat162float(
+            *reinterpret_cast<const __nv_bfloat16*>(win_chunk(win, F.row_lane + r, c) + (dim & 7) * 2));
+      const __nv_bfloat16 hi = __float2bfloat16_rn(acc);
+      const __nv_bfloat16 lo = __float2bfloat16_rn(acc - __bfloat162float(hi));
+      *reinterpret_cast<__nv_bfloat16*>(win_chunk(win, F.qbar_lane, c) + (dim & 7) * 2) = hi;
+      *reinterpret_cast<__nv_bfloat16*>(win_chunk(win, F.qbar_lane + 1, c) + (dim & 7) * 2) = lo;
+    }
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot + H.col;
+
+  if (role == kProdK || role == kProdV) {
+    // ------------------------------------------------------ producers ----
+    if (lane == 0) {
+      const bool is_k = role == kProdK;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      const CUtensorMap* map = is_k ? &map_k : &map_v;
+      for (int t = 0; t < n_tiles; ++t) {
+        const int s = t & 1;
+        if (t >= 2 && !mbar_wait(&empty[s], ((t - 2) >> 1) & 1, p.status, kAttnKernelId)) {
+          *fail = 1;
+          break;
+        }
+        const int y = it.seq * p.seqlen_max + c0 + t * kKeyTile;
+        uint8_t* dst = (is_k ? H.k : H.v) + s * kTileBytes;
+        mbar_arrive_expect_tx(&full[s], kTileBytes);
+        tma_load_2d(dst, map, head * kHD, y, &full[s]);
+        tma_load_2d(dst + kHalfBytes, map, head * kHD + 64, y, &full[s]);
+      }
+    }
+  } else if (role == kMma) {
+    // ------------------------------------------------------------ MMA ----
+    if (lane == 0) {
+      const uint32_t idesc_s = umma_idesc_bf16(128, kKeyTile);
+      const uint32_t idesc_pv = umma_idesc_bf16(128, kHD) | kUmmaBMajorMN;
+      // descriptors of the operand bases; +16 B adds 1 to the start field
+      const uint64_t dq0 = umma_desc_kmajor_sw128(smem_u32(H.q_win0));
+      const uint64_t dq1 = umma_desc_kmajor_sw128(smem_u32(H.q_win1));
+      auto pv = [&](int u) -> bool {
+        const int b = u & 1;
+        if (!mbar_wait(&p_full[b], (u >> 1) & 1, p.status, kAttnKernelId)) return false;
+        if (!mbar_wait(&v_full[b], (u >> 1) & 1, p.status, kAttnKernelId)) return false;
+        tc_fence_after();
+        const uint64_t pa = umma_desc_kmajor_sw128(smem_u32(H.p_win + b * kTcPBytes));
+        const uint64_t va = umma_desc_mnmajor_sw128(smem_u32(H.v + b * kTileBytes), kHalfBytes);
+#pragma unroll
+        for (int kk = 0; kk < kKeyTile / 16; ++kk)
+          umma_bf16(tmem + 128, pa + (kk * 32 >> 4), va + (kk * 2048 >> 4), idesc_pv, (u > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&pv_done[b]);
+        umma_commit(&v_empty[b]);
+        return true;
+      };
+      bool ok = true;
+      for (int t = 0; t < n_tiles && ok; ++t) {
+        const int s = t & 1;
+        ok = mbar_wait(&k_full[s], (t >> 1) & 1, p.status, kAttnKernelId) &&
+             (t < 2 || mbar_wait(&s_empty[s], ((t - 2) >> 1) & 1, p.status, kAttnKernelId));
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t ka = umma_desc_kmajor_sw128(smem_u32(H.k + s * kTileBytes));
+#pragma unroll
+        for (int kk = 0; kk < kHD / 16; ++kk)
+          umma_bf16(tmem + kKeyTile * s, ((kk >> 2) ? dq1 : dq0) + ((kk & 3) * 32 >> 4),
+                    ka + (((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[s]);
+        umma_commit(&k_empty[s]);
+        if (t >= 1) ok = pv(t - 1);
+      }
+      if (ok && n_tiles > 0) ok = pv(n_tiles - 1);
+      if (!ok) *fail = 1;
+      // every issued MMA has completed before TMEM can be released
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.status, kAttnKernelId);
+    }
+  } else if (role == kScores) {
+    // ------------------------------------------------------- scores ----
+    if (scores_on) {
+      float* srow = p.scores + static_cast<int64_t>(it.seq) * p.seqlen_max;
+      const uint32_t taddr = tmem + (H.qbar_lane << 16);  // lanes qbar, qbar+1 = hi, lo
+      for (int t = 0; t < n_tiles; ++t) {
+        const int b = t & 1;
+        if (!mbar_wait(&s_full[b], (t >> 1) & 1, p.status, kAttnKernelId)) {
+          *fail = 1;
+          break;
+        }
+        tc_fence_after();
+        float sc[64];
+        tmem_ld_32x32b_x32(taddr + kKeyTile * b, *reinterpret_cast<float(*)[32]>(&sc[0]));
+        tmem_ld_32x32b_x32(taddr + kKeyTile * b + 32, *reinterpret_cast<float(*)[32]>(&sc[32]));
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[b]);
+#pragma unroll
+        for (int j = 0; j < 64; ++j) sc[j] += __shfl_down_sync(0xffffffffu, sc[j], 1);  // hi + lo
+        if (lane == 0) {
+#pragma unroll
+          for (int j = 0; j < 64; j += 4)
+            *reinterpret_cast<float4*>(H.scr + j) = make_float4(sc[j], sc[j + 1], sc[j + 2], sc[j + 3]);
+        }
+        __syncwarp();
+        const int n0 = c0 + t * kKeyTile;
+        const int n_valid = c1 - n0;
+        if (lane < n_valid) atomicAdd(srow + n0 + lane, H.scr[lane] * p.score_scale);
+        if (lane + 32 < n_valid) atomicAdd(srow + n0 + lane + 32, H.scr[lane + 32] * p.score_scale);
+        __syncwarp();
+      }
+    }
+  } else {
+    // ------------------------------------------------------- softmax ----
+    const int r = (warp & 1) * 32 + lane;  // item row
+    const bool row_ok = has_item && r < it.rows;
+    const uint32_t trow = tmem + ((H.row_lane + static_cast<uint32_t>((warp & 1) * 32)) << 16);
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int t = 0; t < n_tiles; ++t) {
+      const int b = t & 1;
+      ok = mbar_wait(&s_full[b], (t >> 1) & 1, p.status, kAttnKernelId);
+      if (!ok) break;
+      tc_fence_after();
+      float sv[64];
+      tmem_ld_32x32b_x32(trow + kKeyTile * b, *reinterpret_cast<float(*)[32]>(&sv[0]));
+      tmem_ld_32x32b_x32(trow + kKeyTile * b + 32, *reinterpret_cast<float(*)[32]>(&sv[32]));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[b]);
+
+      const int n0 = c0 + t * kKeyTile;
+      const int n_valid = c1 - n0;
+      const bool full = n_valid >= kKeyTile;  // uniform: no per-key mask
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (full || j < n_valid) mx[j & 7] = fmaxf(mx[j & 7], sv[j]);
+#pragma unroll
+      for (int i = 4; i > 0; i >>= 1)
+#pragma unroll
+        for (int k = 0; k < i; ++k) mx[k] = fmaxf(mx[k], mx[k + i]);
+      const float mt = mx[0] * p.scale_log2;  // scale > 0; -inf stays -inf
+      const float m_new = fmaxf(m_used, mt);
+      const bool need = row_ok && m_new > m_used + kTcRescaleThreshold;
+      const float alpha = need ? exp2f(m_used - m_new) : 1.f;  // m_used = -inf -> 0
+      // O holds PV(0..t-1): rescale it when a row of the warp moves its max
+      if (__any_sync(0xffffffffu, need) && t > 0) {
+        ok = mbar_wait(&pv_done[(t - 1) & 1], ((t - 1) >> 1) & 1, p.status, kAttnKernelId);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < kHD / 32; ++c) {
+          float ov[32];
+          tmem_ld_32x32b_x32(trow + 128 + 32 * c, ov);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ov[j] *= alpha;
+          tmem_st_32x32b_x32(trow + 128 + 32 * c, ov);
+        }
+      }
+      if (need) {
+        l *= alpha;
+        m_used = m_new;
+      }
+      const float nref = -(m_used == -INFINITY ? 0.f : m_used);
+      const float scale = p.scale_log2;
+      // p = 2^(s * scale - ref), masked keys 0
+      float ps[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        sv[j] = (full || j < n_valid) ? ex2_approx(fmaf(sv[j], scale, nref)) : 0.f;
+        ps[j & 7] += sv[j];
+      }
+#pragma unroll
+      for (int i = 4; i > 0; i >>= 1)
+#pragma unroll
+        for (int k = 0; k < i; ++k) ps[k] += ps[k + i];
+      l += ps[0];
+      // P buffer b was last read by PV(t-2)
+      if (t >= 2) {
+        ok = mbar_wait(&pv_done[b], ((t - 2) >> 1) & 1, p.status, kAttnKernelId);
+        if (!ok) break;
+      }
+      uint8_t* prow = H.p_row0 + b * kTcPBytes + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+            make_uint4(pack_bf16x2(sv[8 * c], sv[8 * c + 1]), pack_bf16x2(sv[8 * c + 2], sv[8 * c + 3]),
+                       pack_bf16x2(sv[8 * c + 4], sv[8 * c + 5]), pack_bf16x2(sv[8 * c + 6], sv[8 * c + 7]));
+      if (!full) {
+        // TMA brought whole rows past the end of this key range: zero their V
+        // so 0-probability keys cannot inject non-finite cache contents.
+        ok = mbar_wait(&v_full[b], (t >> 1) & 1, p.status, kAttnKernelId);
+        if (!ok) break;
+        for (int idx = r; idx < (kKeyTile - n_valid) * 16; idx += 64) {
+          const int key = n_valid + idx / 16, chunk = idx % 16;
+          *reinterpret_cast<uint4*>(H.v + b * kTileBytes + tile_off(key, chunk)) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+    }
+    if (!ok) *fail = 1;
+
+    // ------------------------------------------------------ epilogue ----
+    const bool have_o = ok && n_tiles > 0 &&
+                        mbar_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, p.status, kAttnKernelId);
+    if (have_o) tc_fence_after();
+    if (has_item) {
+      const int64_t grow = row_ok ? item_row(it, r) : 0;
+      if (p.kv_splits == 1) {
+        const float inv = (have_o && l > 0.f) ? 1.f / l : 0.f;
+        __nv_bfloat16* orow = p.o + grow * d + head * kHD;
+#pragma unroll 1
+        for (int c = 0; c < kHD / 32; ++c) {
+          float ov[32];
+          if (have_o) {
+            tmem_ld_32x32b_x32(trow + 128 + 32 * c, ov);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ov[j] = 0.f;
+          }
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 v;
+              v.x = pack_bf16x2(ov[j] * inv, ov[j + 1] * inv);
+              v.y = pack_bf16x2(ov[j + 2] * inv, ov[j + 3] * inv);
+              v.z = pack_bf16x2(ov[j + 4] * inv, ov[j + 5] * inv);
+              v.w = pack_bf16x2(ov[j + 6] * inv, ov[j + 7] * inv);
+              *reinterpret_cast<uint4*>(orow + 32 * c + j) = v;
+            }
+          }
+        }
+      } else {
+        const int64_t slot = (static_cast<int64_t>(item_id) * p.n_heads + head) * p.kv_splits + split;
+        float* po = p.part_o + (slot * kItemRows + r) * kHD;
+#pragma unroll 1
+        for (int c = 0; c < kHD / 32; ++c) {
+          float ov[32];
+          if (have_o) {
+            tmem_ld_32x32b_x32(trow + 128 + 32 * c, ov);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ov[j] = 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(po + 32 * c + j) = make_float4(ov[j], ov[j + 1], ov[j + 2], ov[j + 3]);
+        }
+        *reinterpret_cast<float2*>(p.part_ml + (slot * kItemRows + r) * 2) =
+            make_float2(have_o ? m_used : -INFINITY, have_o ? l : 0.f);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(*tmem_slot, kTcTmemCols);
+  }
+}
+
 // Merge split-KV partials: O = sum_s 2^(m_s - m) O_s / sum_s 2^(m_s - m) l_s.
 template <bool kVerify>
 __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnParams p) {
@@ -607,15 +1083,32 @@ size_t attn_ws_bytes(int32_t items, int32_t heads, int32_t splits) {
   return align_up(slots * kItemRows * kHD * sizeof(float), 256) + slots * kItemRows * 2 * sizeof(float);
 }
 
+// The cache attention runs on the tcgen05 kernel; FDLLM_ATTN_MMA_SYNC=1
+// selects the mma.sync kernel instead (kept as the comparison point).
+bool use_tc_cache_attention() {
+  static const bool tc = env_int("FDLLM_ATTN_MMA_SYNC", 0) == 0;
+  return tc;
+}
+
 template <bool kVerify>
 int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, AttnParams& p, int grid_items, void* ws,
                 size_t ws_bytes, cudaStream_t stream) {
   static bool attr[64] = {false};
+  const bool tc = !kVerify && use_tc_cache_attention();
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr[dev]) {
+    // Two CTAs per SM need the largest shared-memory carveout; the driver's
+    // default split can leave room for one only.
     if (cudaFuncSetAttribute(attn_kernel<kVerify>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem) !=
-        cudaSuccess)
+            cudaSuccess ||
+        cudaFuncSetAttribute(attn_kernel<kVerify>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+      return FDLLM_ERR_CUDA;
+    if (!kVerify &&
+        (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess ||
+         cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                              cudaSharedmemCarveoutMaxShared) != cudaSuccess))
       return FDLLM_ERR_CUDA;
     attr[dev] = true;
   }
@@ -626,8 +1119,10 @@ int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, AttnParams& p, int
     p.part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) +
                                          align_up(slots * kItemRows * kHD * sizeof(float), 256));
   }
-  dim3 grid(grid_items, p.n_heads, p.kv_splits);
-  attn_kernel<kVerify><<<grid, kAttnThreads, kAttnSmem, stream>>>(mk, mv, p);
+  if (tc)  // one CTA = two work items
+    attn_tc_kernel<<<dim3((grid_items + 1) / 2, p.n_heads, p.kv_splits), kTcThreads, kTcSmem, stream>>>(mk, mv, p);
+  else
+    attn_kernel<kVerify><<<dim3(grid_items, p.n_heads, p.kv_splits), kAttnThreads, kAttnSmem, stream>>>(mk, mv, p);
   if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
   if (p.kv_splits > 1) {
     attn_combine_kernel<kVerify><<<dim3(grid_items, p.n_heads), 256, 0, stream>>>(p);

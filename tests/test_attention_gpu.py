@@ -119,6 +119,29 @@ def test_cache_attention_block128_masked_spans_items():
     assert _rel(sc, so) <= SCORE_TOL
 
 
+@pytest.mark.parametrize("kv_splits", [1, 2])
+def test_cache_attention_growing_logits_and_nan_tail(kv_splits):
+    """Key ranges that end inside a 64-key tile, logits that keep growing
+    along the keys (the running max moves by far more than 2^8 several times),
+    and NaN cache rows past every sequence's key range (never read as keys,
+    zero-probability rows must not leak into the output)."""
+    B, bm, lmax, H = 3, 32, 384, 2
+    k_ends = [77, 200, 333]
+    q, kc, vc, mb, tb, n = _cache_inputs(k_ends, [bm, bm, 20], [5, 40, 0], H * 128, lmax, bm, seed=8)
+    grow = (1.0 + torch.arange(lmax, dtype=torch.float32) / 20.0).repeat(B)[:, None]
+    kc = (kc.float() * grow).bfloat16()
+    for j, ke in enumerate(k_ends):
+        kc[j * lmax + ke:(j + 1) * lmax] = float("nan")
+        vc[j * lmax + ke:(j + 1) * lmax] = float("nan")
+    o, sc = _run_cache(q, kc, vc, mb, tb, n, lmax, bm, H, B, kv_splits)
+    assert torch.isfinite(o).all()
+    oo, so = _oracle_cache(q, kc, vc, mb, tb, lmax, bm, H, B)
+    assert _rel(o, oo) <= TOL
+    sc_valid = torch.cat([sc.cpu()[j * lmax:j * lmax + ke] for j, ke in enumerate(k_ends)])
+    so_valid = torch.cat([so[j * lmax:j * lmax + ke] for j, ke in enumerate(k_ends)])
+    assert _rel(sc_valid, so_valid) <= SCORE_TOL
+
+
 def test_malformed_table_is_reported():
     import flash_dllm_b200.ops as ops
     from flash_dllm_b200._lib import FdllmError, check_device_status
