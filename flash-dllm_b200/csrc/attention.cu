@@ -466,13 +466,15 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 }
 
 // ---------------------------------------------------------------------------
-// tcgen05 cache attention.  Same work items, key slicing, split-KV partial
-// format and results as attn_kernel<false>, with the products on the
-// 5th-generation tensor cores: S = Q K^T and O += P V are M=128 UMMAs issued
-// by one thread, S (double-buffered) and the O accumulator live in tensor
-// memory, and only P passes through shared memory (bf16, 128-byte swizzled:
-// the A operand of the second product).  V is read in place as an MN-major B
-// operand.
+// tcgen05 attention (Flash-Cache and Flash-Verify).  Same work items, key
+// slicing, split-KV partial format and results as attn_kernel, with the
+// products on the 5th-generation tensor cores: S = Q K^T and O += P V are
+// M=128 UMMAs issued by one thread, S (double-buffered) and the O accumulator
+// live in tensor memory, and only P passes through shared memory (bf16,
+// 128-byte swizzled: the A operand of the second product).  V is read in
+// place as an MN-major B operand.  Cache items stream contiguous K/V ranges
+// with TMA; verify items gather theirs with cp.async (the pos_k list, then
+// the block's own k1 / v1 rows under the verify mask).
 //
 // A kernel that uses tensor memory runs one CTA per SM, so each CTA runs two
 // independent pipelines ("halves"), each on its own work item (items 2x and
@@ -562,6 +564,7 @@ __device__ __forceinline__ uint8_t* win_chunk(uint8_t* win, int row, int c) {
   return win + row * 128 + (((c & 7) ^ (row & 7)) << 4);
 }
 
+template <bool kVerify>
 __global__ void __launch_bounds__(kTcThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                    const AttnParams p) {
@@ -595,20 +598,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // this half's work item
   const int item_id = 2 * blockIdx.x + h;
   Item it{};
-  const bool has_item = load_item(p, false, item_id, it);
-  int c0 = 0, c1 = 0, n_tiles = 0;
+  const bool has_item = load_item(p, kVerify, item_id, it);
+  // keys of this split: equal 64-aligned slices of the item's cache keys;
+  // verify items add their block's own keys (last split) as further tiles
+  int c0 = 0, c1 = 0, nt_cache = 0, n_tiles = 0;
   if (has_item) {
     const int per = ((it.n_keys + p.kv_splits - 1) / p.kv_splits + kKeyTile - 1) / kKeyTile * kKeyTile;
     c0 = min(it.n_keys, split * per);
     c1 = min(it.n_keys, c0 + per);
-    n_tiles = (c1 - c0 + kKeyTile - 1) / kKeyTile;
+    nt_cache = (c1 - c0 + kKeyTile - 1) / kKeyTile;
+    const int nt_blk = (kVerify && split == p.kv_splits - 1) ? (it.blk_rows + kKeyTile - 1) / kKeyTile : 0;
+    n_tiles = nt_cache + nt_blk;
   }
-  const bool scores_on = has_item && p.scores != nullptr && it.m_len > 0;
+  const bool scores_on = !kVerify && has_item && p.scores != nullptr && it.m_len > 0;
   const int64_t d = p.d_model;
   {
     // the CTA exits only when neither half has an item
     Item other{};
-    const bool other_has = load_item(p, false, 2 * blockIdx.x + (1 - h), other);
+    const bool other_has = load_item(p, kVerify, 2 * blockIdx.x + (1 - h), other);
     if (!has_item && !other_has) return;  // uniform across the CTA
   }
 
@@ -629,7 +636,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   if (warp == 8) {
     tmem_alloc(tmem_slot, kTcTmemCols);
-    if (lane == 0) {
+    if (!kVerify && lane == 0) {  // verify mode gets no tensor maps
       tma_prefetch_desc(&map_k);
       tma_prefetch_desc(&map_v);
     }
@@ -641,7 +648,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int f = threadIdx.x >> 7, tid = threadIdx.x & 127;
     const TcHalf F = tc_half(smem, f);
     Item fi{};
-    const bool f_has = load_item(p, false, 2 * blockIdx.x + f, fi);
+    const bool f_has = load_item(p, kVerify, 2 * blockIdx.x + f, fi);
     constexpr int kPer = kItemRows * 16 / 128;
     uint4 v[kPer];
 #pragma unroll
@@ -660,7 +667,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int hh = tid >> 6, rr = F.qbar_lane + ((tid >> 3) & 7), ch = tid & 7;
       *reinterpret_cast<uint4*>(win_chunk(hh ? F.q_win1 : F.q_win0, rr, ch)) = make_uint4(0, 0, 0, 0);
     }
-    const bool f_scores = f_has && p.scores != nullptr && fi.m_len > 0;
+    const bool f_scores = !kVerify && f_has && p.scores != nullptr && fi.m_len > 0;
     if (f_scores) {
       // qbar dim = tid: fp32 sum over the masked rows (the item's first m_len
       // rows) -> bf16 hi (row qbar_lane) and lo (row qbar_lane + 1)
@@ -686,8 +693,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot + H.col;
 
-  if (role == kProdK || role == kProdV) {
-    // ------------------------------------------------------ producers ----
+  if ((role == kProdK || role == kProdV) && !kVerify) {
+    // ------------------------------------------------- TMA producers ----
     if (lane == 0) {
       const bool is_k = role == kProdK;
       uint64_t* full = is_k ? k_full : v_full;
@@ -706,6 +713,68 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tma_load_2d(dst + kHalfBytes, map, head * kHD + 64, y, &full[s]);
       }
     }
+  } else if (role == kProdK || role == kProdV) {
+    // ---------------------------------------------- gather producers ----
+    // Verify keys: cache rows listed in pos_k, then the block's own rows of
+    // k1 / v1.  16-byte cp.async per lane, zero-filled for missing keys; tile
+    // t is published once the copies of t+1 are in flight.
+    const bool is_k = role == kProdK;
+    uint64_t* full = is_k ? k_full : v_full;
+    uint64_t* empty = is_k ? k_empty : v_empty;
+    bool ok = true;
+    for (int t = 0; t < n_tiles; ++t) {
+      const int s = t & 1;
+      if (t >= 2 && !mbar_wait(&empty[s], ((t - 2) >> 1) & 1, p.status, kAttnKernelId)) {
+        ok = false;
+        break;
+      }
+      const bool blk = t >= nt_cache;
+      const int n0 = blk ? (t - nt_cache) * kKeyTile : c0 + t * kKeyTile;
+      const int n_end = blk ? it.blk_rows : c1;
+      int64_t src_row[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int n = n0 + lane + 32 * hh;
+        int64_t row = -1;
+        if (n < n_end) {
+          if (blk) {
+            row = it.blk_q0 + n;
+          } else {
+            const int64_t pk = static_cast<int64_t>(it.k_base) + n;
+            row = (pk < p.n_pos_k) ? p.pos_k[pk] : -1;
+            if (row < 0 || row >= p.n_slots) {
+              if (is_k) report(p.status, FDLLM_ERR_INDEX, static_cast<int>(pk), kAttnKernelId);
+              row = -1;
+            }
+          }
+        }
+        src_row[hh] = row;
+      }
+      const __nv_bfloat16* src = is_k ? (blk ? p.k1 : p.kc) : (blk ? p.v1 : p.vc);
+      uint8_t* dst = (is_k ? H.k : H.v) + s * kTileBytes;
+#pragma unroll 8
+      for (int i = 0; i < kKeyTile / 2; ++i) {
+        const int key = 2 * i + (lane >> 4);
+        const int chunk = lane & 15;
+        const int64_t r0 = __shfl_sync(0xffffffffu, src_row[0], key & 31);
+        const int64_t r1 = __shfl_sync(0xffffffffu, src_row[1], key & 31);
+        const int64_t row = key < 32 ? r0 : r1;
+        const bool valid = row >= 0;
+        cp_async_16_zfill(dst + tile_off(key, chunk), src + (valid ? row * d + head * kHD + chunk * 8 : 0), valid);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      if (t >= 1) {
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[(t - 1) & 1]);
+      }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (ok && n_tiles > 0 && lane == 0) mbar_arrive(&full[(n_tiles - 1) & 1]);
+    if (!ok) *fail = 1;
   } else if (role == kMma) {
     // ------------------------------------------------------------ MMA ----
     if (lane == 0) {
@@ -788,6 +857,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int r = (warp & 1) * 32 + lane;  // item row
     const bool row_ok = has_item && r < it.rows;
     const uint32_t trow = tmem + ((H.row_lane + static_cast<uint32_t>((warp & 1) * 32)) << 16);
+    const uint8_t* mrow = nullptr;  // verify: this row's in-block mask
+    if (kVerify && has_item) {
+      const int64_t base = static_cast<int64_t>(it.seq) * p.block_rows + it.chunk_row0;
+      mrow = p.mask + (base + min(r, max(it.rows - 1, 0))) * p.block_rows;
+    }
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
@@ -802,15 +876,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[b]);
 
-      const int n0 = c0 + t * kKeyTile;
-      const int n_valid = c1 - n0;
-      const bool full = n_valid >= kKeyTile;  // uniform: no per-key mask
+      const bool blk = kVerify && t >= nt_cache;
+      const int n0 = blk ? (t - nt_cache) * kKeyTile : c0 + t * kKeyTile;
+      const int n_valid = (blk ? it.blk_rows : c1) - n0;
+      const bool full = n_valid >= kKeyTile;  // uniform
+      if (blk) {
+        // the block's own keys: key range and the verify mask of this row
+#pragma unroll
+        for (int j = 0; j < 64; ++j) sv[j] = (j < n_valid && __ldg(mrow + n0 + j) != 0) ? sv[j] : -INFINITY;
+      } else if (!full) {
+        // keys past the range: -inf logits (probability 0 below)
+#pragma unroll
+        for (int j = 0; j < 64; ++j) sv[j] = j < n_valid ? sv[j] : -INFINITY;
+      }
       float mx[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+      for (int i = 0; i < 8; ++i) mx[i] = sv[i];
 #pragma unroll
-      for (int j = 0; j < 64; ++j)
-        if (full || j < n_valid) mx[j & 7] = fmaxf(mx[j & 7], sv[j]);
+      for (int j = 8; j < 64; ++j) mx[j & 7] = fmaxf(mx[j & 7], sv[j]);
 #pragma unroll
       for (int i = 4; i > 0; i >>= 1)
 #pragma unroll
@@ -845,7 +928,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int i = 0; i < 8; ++i) ps[i] = 0.f;
 #pragma unroll
       for (int j = 0; j < 64; ++j) {
-        sv[j] = (full || j < n_valid) ? ex2_approx(fmaf(sv[j], scale, nref)) : 0.f;
+        sv[j] = ex2_approx(fmaf(sv[j], scale, nref));  // -inf -> 0
         ps[j & 7] += sv[j];
       }
 #pragma unroll
@@ -864,7 +947,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
             make_uint4(pack_bf16x2(sv[8 * c], sv[8 * c + 1]), pack_bf16x2(sv[8 * c + 2], sv[8 * c + 3]),
                        pack_bf16x2(sv[8 * c + 4], sv[8 * c + 5]), pack_bf16x2(sv[8 * c + 6], sv[8 * c + 7]));
-      if (!full) {
+      if (!kVerify && !full) {
         // TMA brought whole rows past the end of this key range: zero their V
         // so 0-probability keys cannot inject non-finite cache contents.
         ok = mbar_wait(&v_full[b], (t >> 1) & 1, p.status, kAttnKernelId);
@@ -1083,9 +1166,9 @@ size_t attn_ws_bytes(int32_t items, int32_t heads, int32_t splits) {
   return align_up(slots * kItemRows * kHD * sizeof(float), 256) + slots * kItemRows * 2 * sizeof(float);
 }
 
-// The cache attention runs on the tcgen05 kernel; FDLLM_ATTN_MMA_SYNC=1
-// selects the mma.sync kernel instead (kept as the comparison point).
-bool use_tc_cache_attention() {
+// Attention runs on the tcgen05 kernel; FDLLM_ATTN_MMA_SYNC=1 selects the
+// mma.sync kernel instead (kept as the comparison point).
+bool use_tc_attention() {
   static const bool tc = env_int("FDLLM_ATTN_MMA_SYNC", 0) == 0;
   return tc;
 }
@@ -1094,7 +1177,7 @@ template <bool kVerify>
 int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, AttnParams& p, int grid_items, void* ws,
                 size_t ws_bytes, cudaStream_t stream) {
   static bool attr[64] = {false};
-  const bool tc = !kVerify && use_tc_cache_attention();
+  const bool tc = use_tc_attention();
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr[dev]) {
@@ -1105,10 +1188,10 @@ int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, AttnParams& p, int
         cudaFuncSetAttribute(attn_kernel<kVerify>, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       return FDLLM_ERR_CUDA;
-    if (!kVerify &&
-        (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess ||
-         cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                              cudaSharedmemCarveoutMaxShared) != cudaSuccess))
+    if (cudaFuncSetAttribute(attn_tc_kernel<kVerify>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(attn_tc_kernel<kVerify>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       return FDLLM_ERR_CUDA;
     attr[dev] = true;
   }
@@ -1120,7 +1203,8 @@ int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, AttnParams& p, int
                                          align_up(slots * kItemRows * kHD * sizeof(float), 256));
   }
   if (tc)  // one CTA = two work items
-    attn_tc_kernel<<<dim3((grid_items + 1) / 2, p.n_heads, p.kv_splits), kTcThreads, kTcSmem, stream>>>(mk, mv, p);
+    attn_tc_kernel<kVerify>
+        <<<dim3((grid_items + 1) / 2, p.n_heads, p.kv_splits), kTcThreads, kTcSmem, stream>>>(mk, mv, p);
   else
     attn_kernel<kVerify><<<dim3(grid_items, p.n_heads, p.kv_splits), kAttnThreads, kAttnSmem, stream>>>(mk, mv, p);
   if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
