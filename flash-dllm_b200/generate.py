@@ -19,12 +19,19 @@ verify step whose masked window is cut short by the end of the slot buffer
 (generate.py:215 slices a full window and the assignment at :235 raises) --
 the actual window length is used.
 
+Forwards whose input shapes repeat are replayed as CUDA graphs.  The KV
+caches, score buffer, RoPE tables and graphs live in a per-model session
+(one per batch size / slot length), so a later call of the same shape zeroes
+the caches and replays the graphs an earlier call captured.
+
 ``min_keep`` (default 1, the reference) forces a minimum number of accepted
 tokens per step; ``trace`` (a list) receives the per-step decisions.
 """
 from __future__ import annotations
 
 from typing import List, Optional
+
+import weakref
 
 import numpy as np
 import torch
@@ -66,6 +73,8 @@ class _Forwarder:
         self.enabled = enabled
         self.seen = {}
         self.graphs = {}
+        self.pool = None
+        self.stream = None
 
     def __call__(self, key, inputs: dict, build):
         if not self.enabled:
@@ -82,11 +91,68 @@ class _Forwarder:
             return build(inputs)
         static = {name: t.clone() for name, t in inputs.items()}
         result = build(static)  # this step's real forward; also sizes workspaces
+        # Capture on a side stream into one memory pool shared by all of this
+        # generation's graphs.  (torch.cuda.graph would also run gc and empty
+        # the allocator cache before every capture: ~0.5 s each.)
+        if self.pool is None:
+            self.pool = torch.cuda.graph_pool_handle()
+            self.stream = torch.cuda.Stream()
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            out = build(static)
+        cur = torch.cuda.current_stream()
+        self.stream.wait_stream(cur)
+        with torch.cuda.stream(self.stream):
+            graph.capture_begin(pool=self.pool)
+            try:
+                out = build(static)
+            finally:
+                graph.capture_end()
+        cur.wait_stream(self.stream)
         self.graphs[key] = (static, graph, out)
         return result
+
+
+class _Session:
+    """Device state one model keeps between generate calls of the same shape
+    (batch size, slot length, dtype, device): the per-layer KV caches, the
+    attention-score buffer, the RoPE tables and the CUDA graphs of the
+    forwards, which all reference these buffers.  A call zeroes the caches
+    and scores instead of allocating them, so forwards captured by an earlier
+    call replay unchanged."""
+
+    def __init__(self, model, B: int, L: int, head_dim: int, use_graphs: bool):
+        dev, cfg = model.device, model.config
+        self.caches = [(torch.zeros((L * B, cfg.d_model), dtype=model.dtype, device=dev),
+                        torch.zeros((L * B, cfg.d_model), dtype=model.dtype, device=dev))
+                       for _ in model.model.transformer.blocks]
+        self.attn_scores = torch.zeros(B * L, dtype=torch.float32, device=dev)
+        sin, cos = get_rotary_embedding(L, head_dim, cfg.rope_theta, dev)
+        self.rotary = [sin.repeat(B, 1).contiguous(), cos.repeat(B, 1).contiguous()]
+        self.empty_i32 = torch.zeros(0, device=dev, dtype=torch.int32)
+        self.empty_i64 = torch.zeros(0, device=dev, dtype=torch.int64)
+        self.forward = _Forwarder(use_graphs and dev.type == "cuda")
+
+    def reset(self, model) -> None:
+        for block, (kc, vc) in zip(model.model.transformer.blocks, self.caches):
+            kc.zero_()
+            vc.zero_()
+            block.k_cache, block.v_cache = kc, vc
+        self.attn_scores.zero_()
+
+
+_SESSIONS = weakref.WeakKeyDictionary()
+
+
+def _session(model, B: int, L: int, head_dim: int, use_graphs: bool) -> _Session:
+    key = (B, L, model.dtype, str(model.device), use_graphs)
+    held = _SESSIONS.get(model)
+    if held is None or held[0] != key:
+        held = (key, None)
+        _SESSIONS[model] = held  # drop the previous shape's buffers first
+        held = (key, _Session(model, B, L, head_dim, use_graphs))
+        _SESSIONS[model] = held
+    sess = held[1]
+    sess.reset(model)
+    return sess
 
 
 class _Slots:
@@ -142,18 +208,14 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
     x = torch.full((B * L,), mask_id, dtype=torch.long, device=dev)
     x_draft = torch.full((B * L,), mask_id, dtype=torch.long, device=dev)
     full_pos = torch.arange(B * L, device=dev).reshape(B, L)
-    attn_scores = torch.zeros(B * L, dtype=torch.float32, device=dev)
-    sin, cos = get_rotary_embedding(L, head_dim, cfg.rope_theta, dev)
-    rotary_emb_pos = [sin.repeat(B, 1).contiguous(), cos.repeat(B, 1).contiguous()]
-    for block in model.model.transformer.blocks:
-        block.k_cache = torch.zeros((L * B, d_model), dtype=model.dtype, device=dev)
-        block.v_cache = torch.zeros((L * B, d_model), dtype=model.dtype, device=dev)
-    empty_i32 = torch.tensor([], device=dev, dtype=torch.int32)
-    empty_i64 = torch.tensor([], device=dev, dtype=torch.int64)
+    sess = _session(model, B, L, head_dim, use_graphs)
+    attn_scores = sess.attn_scores
+    rotary_emb_pos = sess.rotary
+    empty_i32, empty_i64 = sess.empty_i32, sess.empty_i64
     masks = [torch.from_numpy(_verify_mask(bm, s)).to(dev) for s in range(bm // 2 + 1)]
     ar_L = torch.arange(L, device=dev)
     st = _Slots(B)
-    forward = _Forwarder(use_graphs and dev.type == "cuda")
+    forward = sess.forward
     count = 0
     start_layer = [-1] * B
 
