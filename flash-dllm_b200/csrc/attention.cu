@@ -477,9 +477,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 // the block's own k1 / v1 rows under the verify mask).
 //
 // A kernel that uses tensor memory runs one CTA per SM, so each CTA runs two
-// independent pipelines ("halves"), each on its own work item (items 2x and
-// 2x+1 of the grid's x index) with its own shared memory, barriers and 256
-// TMEM columns.  A tcgen05.mma costs about the same issue time for any
+// independent pipelines ("halves"), each on its own (item, key split) unit --
+// units 2x and 2x+1 of the grid's x index, unit = item * kv_splits + split --
+// with its own shared memory, barriers and 256 TMEM columns.  A tcgen05.mma costs about the same issue time for any
 // M <= 128 and N <= 128, so each half issues few, wide ones: per 64-key tile
 // one M=128, N=64 S product (8 K-steps) and one M=128, N=128 PV product
 // (4 K-steps).  The 128 rows of a half's S operand are its 64 query rows and
@@ -573,7 +573,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int head = blockIdx.y;
-  const int split = blockIdx.z;
 
   // warp -> (half, role): 0,1 softmax h0 | 2,3 softmax h1 | 4 scores h1 |
   // 5 MMA h0 | 6 scores h0 | 7 MMA h1 | 8 K h0 | 9 V h0 | 10 K h1 | 11 V h1
@@ -595,8 +594,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kH0Bar + 18 * 8);
   volatile int32_t* fail = reinterpret_cast<volatile int32_t*>(H.bar + 17);
 
-  // this half's work item
-  const int item_id = 2 * blockIdx.x + h;
+  // this half's work unit
+  const int unit = 2 * blockIdx.x + h;
+  const int item_id = unit / p.kv_splits;
+  const int split = unit % p.kv_splits;
   Item it{};
   const bool has_item = load_item(p, kVerify, item_id, it);
   // keys of this split: equal 64-aligned slices of the item's cache keys;
@@ -615,7 +616,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   {
     // the CTA exits only when neither half has an item
     Item other{};
-    const bool other_has = load_item(p, kVerify, 2 * blockIdx.x + (1 - h), other);
+    const bool other_has = load_item(p, kVerify, (2 * blockIdx.x + (1 - h)) / p.kv_splits, other);
     if (!has_item && !other_has) return;  // uniform across the CTA
   }
 
@@ -648,7 +649,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int f = threadIdx.x >> 7, tid = threadIdx.x & 127;
     const TcHalf F = tc_half(smem, f);
     Item fi{};
-    const bool f_has = load_item(p, kVerify, 2 * blockIdx.x + f, fi);
+    const bool f_has = load_item(p, kVerify, (2 * blockIdx.x + f) / p.kv_splits, fi);
     constexpr int kPer = kItemRows * 16 / 128;
     uint4 v[kPer];
 #pragma unroll
@@ -1203,8 +1204,8 @@ int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, AttnParams& p, int
                                          align_up(slots * kItemRows * kHD * sizeof(float), 256));
   }
   if (tc)  // one CTA = two work items
-    attn_tc_kernel<kVerify>
-        <<<dim3((grid_items + 1) / 2, p.n_heads, p.kv_splits), kTcThreads, kTcSmem, stream>>>(mk, mv, p);
+    attn_tc_kernel<kVerify>  // one CTA = two (item, split) units
+        <<<dim3((grid_items * p.kv_splits + 1) / 2, p.n_heads, 1), kTcThreads, kTcSmem, stream>>>(mk, mv, p);
   else
     attn_kernel<kVerify><<<dim3(grid_items, p.n_heads, p.kv_splits), kAttnThreads, kAttnSmem, stream>>>(mk, mv, p);
   if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
