@@ -567,6 +567,7 @@ __device__ __forceinline__ uint8_t* win_chunk(uint8_t* win, int row, int c) {
 template <bool kVerify>
 __global__ void __launch_bounds__(kTcThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                   const __grid_constant__ CUtensorMap map_k1, const __grid_constant__ CUtensorMap map_v1,
                    const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -637,9 +638,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   if (warp == 8) {
     tmem_alloc(tmem_slot, kTcTmemCols);
-    if (!kVerify && lane == 0) {  // verify mode gets no tensor maps
+    if (lane == 0) {
       tma_prefetch_desc(&map_k);
       tma_prefetch_desc(&map_v);
+      if (kVerify) {
+        tma_prefetch_desc(&map_k1);
+        tma_prefetch_desc(&map_v1);
+      }
     }
   }
   if (warp < 8) {
@@ -717,12 +722,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (role == kProdK || role == kProdV) {
     // ---------------------------------------------- gather producers ----
     // Verify keys: cache rows listed in pos_k, then the block's own rows of
-    // k1 / v1.  16-byte cp.async per lane, zero-filled for missing keys; tile
-    // t is published once the copies of t+1 are in flight.
+    // k1 / v1.  A tile whose 64 keys are 64 consecutive rows (the common case:
+    // the key list is a few runs of cache slots) is one pair of TMA boxes;
+    // any other tile is gathered with 16-byte cp.async per lane, zero-filled
+    // for missing keys, and published once the copies of the next gathered
+    // tile are in flight.
     const bool is_k = role == kProdK;
     uint64_t* full = is_k ? k_full : v_full;
     uint64_t* empty = is_k ? k_empty : v_empty;
     bool ok = true;
+    int pending = -1;  // gathered tile not yet published
     for (int t = 0; t < n_tiles; ++t) {
       const int s = t & 1;
       if (t >= 2 && !mbar_wait(&empty[s], ((t - 2) >> 1) & 1, p.status, kAttnKernelId)) {
@@ -751,8 +760,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         src_row[hh] = row;
       }
-      const __nv_bfloat16* src = is_k ? (blk ? p.k1 : p.kc) : (blk ? p.v1 : p.vc);
       uint8_t* dst = (is_k ? H.k : H.v) + s * kTileBytes;
+      const int64_t row0 = __shfl_sync(0xffffffffu, src_row[0], 0);
+      const bool run = __all_sync(0xffffffffu, row0 >= 0 && src_row[0] == row0 + lane && src_row[1] == row0 + lane + 32);
+      if (run) {
+        // publish the gathered tile before it, then load this one with TMA
+        if (pending >= 0) {
+          asm volatile("cp.async.wait_group 0;" ::: "memory");
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[pending & 1]);
+          pending = -1;
+        }
+        if (lane == 0) {
+          const CUtensorMap* map = is_k ? (blk ? &map_k1 : &map_k) : (blk ? &map_v1 : &map_v);
+          mbar_arrive_expect_tx(&full[s], kTileBytes);
+          tma_load_2d(dst, map, head * kHD, static_cast<int32_t>(row0), &full[s]);
+          tma_load_2d(dst + kHalfBytes, map, head * kHD + 64, static_cast<int32_t>(row0), &full[s]);
+        }
+        continue;
+      }
+      const __nv_bfloat16* src = is_k ? (blk ? p.k1 : p.kc) : (blk ? p.v1 : p.vc);
 #pragma unroll 8
       for (int i = 0; i < kKeyTile / 2; ++i) {
         const int key = 2 * i + (lane >> 4);
@@ -764,17 +792,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         cp_async_16_zfill(dst + tile_off(key, chunk), src + (valid ? row * d + head * kHD + chunk * 8 : 0), valid);
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
-      if (t >= 1) {
+      if (pending >= 0) {
         asm volatile("cp.async.wait_group 1;" ::: "memory");
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full[(t - 1) & 1]);
+        if (lane == 0) mbar_arrive(&full[pending & 1]);
       }
+      pending = t;
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     fence_proxy_async_smem();
     __syncwarp();
-    if (ok && n_tiles > 0 && lane == 0) mbar_arrive(&full[(n_tiles - 1) & 1]);
+    if (ok && pending >= 0 && lane == 0) mbar_arrive(&full[pending & 1]);
     if (!ok) *fail = 1;
   } else if (role == kMma) {
     // ------------------------------------------------------------ MMA ----
@@ -1175,8 +1204,8 @@ bool use_tc_attention() {
 }
 
 template <bool kVerify>
-int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, AttnParams& p, int grid_items, void* ws,
-                size_t ws_bytes, cudaStream_t stream) {
+int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mk1, const CUtensorMap& mv1,
+                AttnParams& p, int grid_items, void* ws, size_t ws_bytes, cudaStream_t stream) {
   static bool attr[64] = {false};
   const bool tc = use_tc_attention();
   int dev = 0;
@@ -1205,7 +1234,8 @@ int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, AttnParams& p, int
   }
   if (tc)  // one CTA = two work items
     attn_tc_kernel<kVerify>  // one CTA = two (item, split) units
-        <<<dim3((grid_items * p.kv_splits + 1) / 2, p.n_heads, 1), kTcThreads, kTcSmem, stream>>>(mk, mv, p);
+        <<<dim3((grid_items * p.kv_splits + 1) / 2, p.n_heads, 1), kTcThreads, kTcSmem, stream>>>(mk, mv, mk1, mv1,
+                                                                                                  p);
   else
     attn_kernel<kVerify><<<dim3(grid_items, p.n_heads, p.kv_splits), kAttnThreads, kAttnSmem, stream>>>(mk, mv, p);
   if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
@@ -1280,7 +1310,7 @@ int fdllm_attn_cache(const void* q, void* o, const void* k_cache, const void* v_
   p.n_heads = n_heads;
   p.seqlen_max = seqlen_max;
   p.kv_splits = kv_splits;
-  return launch_attn<false>(mk, mv, p, max_items, workspace, workspace_bytes, stream);
+  return launch_attn<false>(mk, mv, mk, mv, p, max_items, workspace, workspace_bytes, stream);
 }
 
 int fdllm_verify_attn(const void* q1, const void* k1, const void* v1, void* o, const void* k_cache,
@@ -1320,9 +1350,14 @@ int fdllm_verify_attn(const void* q1, const void* k1, const void* v1, void* o, c
   p.block_rows = block_rows;
   p.row_chunks = (block_rows + kItemRows - 1) / kItemRows;
   p.n_items = n_blocks * p.row_chunks;
-  CUtensorMap dummy;
-  std::memset(&dummy, 0, sizeof(dummy));
-  return launch_attn<true>(dummy, dummy, p, p.n_items, workspace, workspace_bytes, stream);
+  // tensor maps for tiles whose keys are consecutive rows (TMA instead of a gather)
+  CUtensorMap mk, mv, mk1, mv1;
+  int rc;
+  if ((rc = make_tmap_bf16_sw128(&mk, k_cache, n_slots, d_model, d_model, kKeyTile)) != FDLLM_OK) return rc;
+  if ((rc = make_tmap_bf16_sw128(&mv, v_cache, n_slots, d_model, d_model, kKeyTile)) != FDLLM_OK) return rc;
+  if ((rc = make_tmap_bf16_sw128(&mk1, k1, n_rows, d_model, d_model, kKeyTile)) != FDLLM_OK) return rc;
+  if ((rc = make_tmap_bf16_sw128(&mv1, v1, n_rows, d_model, d_model, kKeyTile)) != FDLLM_OK) return rc;
+  return launch_attn<true>(mk, mv, mk1, mv1, p, p.n_items, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"
