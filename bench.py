@@ -363,16 +363,21 @@ def main():
     if rank == 0:
         hbm, tf, tf_sus, src = _peaks()
         rows = kt["rows"]
+        # DRAM bytes (read + write) of one QKV launch at the 8-sequence step
+        # shape, from the ncu capture summarised in
+        # profiles/qkv_rope_cache_512rows.md; other shapes: not captured
+        traffic = (105.458944e6 + 4.807680e6) if rows == 512 else None
         compute_bound = kt["qkv_flops"] / kt["qkv_bytes"] > (tf * 1e12) / (hbm * 1e9)
         if compute_bound:
             ach = kt["qkv_flops"] / kt["qkv_s"] / 1e12
             roof = {"kernel": "qkv_rope_cache (tcgen05)", "bound": "tensor", "achieved": ach, "peak": tf,
-                    "unit": "TFLOP/s", "frac": ach / tf, "peak_source": src, "traffic": None,
-                    "rows": rows}
+                    "unit": "TFLOP/s", "frac": ach / tf, "peak_source": src, "traffic": traffic,
+                    "traffic_unit": "bytes per launch (ncu)", "rows": rows}
         else:
             ach = kt["qkv_bytes"] / kt["qkv_s"] / 1e9
             roof = {"kernel": "qkv_rope_cache (tcgen05)", "bound": "hbm", "achieved": ach, "peak": hbm,
-                    "unit": "GB/s", "frac": ach / hbm, "peak_source": src, "traffic": None, "rows": rows}
+                    "unit": "GB/s", "frac": ach / hbm, "peak_source": src, "traffic": traffic,
+                    "traffic_unit": "bytes per launch (ncu)", "rows": rows}
         attn_gbs = kt["attn_bytes"] / kt["attn_s"] / 1e9
         line = {
             "metric": METRIC, "value": tok_all / elapsed_all, "unit": "tokens/s", "n_gpus": world,
