@@ -85,6 +85,7 @@ struct AttnParams {
   float* scores;                // cache mode, optional
   float* part_o;                // split-KV partials [item][head][split][64][128]
   float* part_ml;               // [item][head][split][64][2]
+  int32_t* counters;            // tcgen05 kernel: splits done per (item, head), left at 0
   int32_t* status;
   int64_t n_slots;
   int64_t n_pos_k;
@@ -1025,8 +1026,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       } else {
-        const int64_t slot = (static_cast<int64_t>(item_id) * p.n_heads + head) * p.kv_splits + split;
-        float* po = p.part_o + (slot * kItemRows + r) * kHD;
+        // Split of a key range: store this split's unnormalised O row and
+        // (m, l); the last split of the (item, head) to finish merges them:
+        // O = sum_s 2^(m_s - m) O_s / sum_s 2^(m_s - m) l_s.
+        const int64_t pair = static_cast<int64_t>(item_id) * p.n_heads + head;
+        const int64_t slot0 = pair * p.kv_splits;
+        float* po = p.part_o + ((slot0 + split) * kItemRows + r) * kHD;
 #pragma unroll 1
         for (int c = 0; c < kHD / 32; ++c) {
           float ov[32];
@@ -1040,8 +1045,65 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int j = 0; j < 32; j += 4)
             *reinterpret_cast<float4*>(po + 32 * c + j) = make_float4(ov[j], ov[j + 1], ov[j + 2], ov[j + 3]);
         }
-        *reinterpret_cast<float2*>(p.part_ml + (slot * kItemRows + r) * 2) =
+        *reinterpret_cast<float2*>(p.part_ml + ((slot0 + split) * kItemRows + r) * 2) =
             make_float2(have_o ? m_used : -INFINITY, have_o ? l : 0.f);
+        __threadfence();
+        volatile int32_t* last_flag = reinterpret_cast<volatile int32_t*>(H.bar + 19);
+        if (h == 0)
+          asm volatile("bar.sync 3, 64;" ::: "memory");
+        else
+          asm volatile("bar.sync 4, 64;" ::: "memory");
+        if (r == 0) {
+          const int prev = atomicAdd(p.counters + pair, 1);
+          const int last = prev == p.kv_splits - 1 ? 1 : 0;
+          if (last) p.counters[pair] = 0;  // ready for the next call
+          *last_flag = last;
+          __threadfence();
+        }
+        if (h == 0)
+          asm volatile("bar.sync 3, 64;" ::: "memory");
+        else
+          asm volatile("bar.sync 4, 64;" ::: "memory");
+        if (*last_flag != 0 && row_ok) {
+          float mmax = -INFINITY;
+          for (int s2 = 0; s2 < p.kv_splits; ++s2)
+            mmax = fmaxf(mmax, __ldcg(p.part_ml + ((slot0 + s2) * kItemRows + r) * 2));
+          const float ref = mmax == -INFINITY ? 0.f : mmax;
+          float lsum = 0.f;
+          for (int s2 = 0; s2 < p.kv_splits; ++s2) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + ((slot0 + s2) * kItemRows + r) * 2));
+            lsum += exp2f(ml.x - ref) * ml.y;
+          }
+          const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+          __nv_bfloat16* orow = p.o + grow * d + head * kHD;
+#pragma unroll 1
+          for (int c = 0; c < kHD / 32; ++c) {
+            float acc[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+            for (int s2 = 0; s2 < p.kv_splits; ++s2) {
+              const float wgt = exp2f(__ldcg(p.part_ml + ((slot0 + s2) * kItemRows + r) * 2) - ref);
+              const float* src = p.part_o + ((slot0 + s2) * kItemRows + r) * kHD + 32 * c;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src + j));
+                acc[j] += wgt * v4.x;
+                acc[j + 1] += wgt * v4.y;
+                acc[j + 2] += wgt * v4.z;
+                acc[j + 3] += wgt * v4.w;
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 v;
+              v.x = pack_bf16x2(acc[j] * inv, acc[j + 1] * inv);
+              v.y = pack_bf16x2(acc[j + 2] * inv, acc[j + 3] * inv);
+              v.z = pack_bf16x2(acc[j + 4] * inv, acc[j + 5] * inv);
+              v.w = pack_bf16x2(acc[j + 6] * inv, acc[j + 7] * inv);
+              *reinterpret_cast<uint4*>(orow + 32 * c + j) = v;
+            }
+          }
+        }
       }
     }
   }
@@ -1190,10 +1252,16 @@ namespace {
 
 int plan_capacity(int32_t n_rows, int32_t batch) { return (n_rows + kItemRows - 1) / kItemRows + batch; }
 
+// Workspace layout when keys are split: a fixed counter region (one counter
+// per (item, head), left at zero after every call, at the same place for
+// every call), then the partial O rows, then the partial (m, l).
+constexpr size_t kAttnCounterBytes = 64 * 1024;
+
 size_t attn_ws_bytes(int32_t items, int32_t heads, int32_t splits) {
   if (splits <= 1) return 256;
   const size_t slots = static_cast<size_t>(items) * heads * splits;
-  return align_up(slots * kItemRows * kHD * sizeof(float), 256) + slots * kItemRows * 2 * sizeof(float);
+  return kAttnCounterBytes + align_up(slots * kItemRows * kHD * sizeof(float), 256) +
+         slots * kItemRows * 2 * sizeof(float);
 }
 
 // Attention runs on the tcgen05 kernel; FDLLM_ATTN_MMA_SYNC=1 selects the
@@ -1227,9 +1295,11 @@ int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap&
   }
   if (p.kv_splits > 1) {
     if (ws == nullptr || ws_bytes < attn_ws_bytes(grid_items, p.n_heads, p.kv_splits)) return FDLLM_ERR_WORKSPACE;
+    if (static_cast<size_t>(grid_items) * p.n_heads * sizeof(int32_t) > kAttnCounterBytes) return FDLLM_ERR_ARG;
     const size_t slots = static_cast<size_t>(grid_items) * p.n_heads * p.kv_splits;
-    p.part_o = static_cast<float*>(ws);
-    p.part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) +
+    p.counters = static_cast<int32_t*>(ws);
+    p.part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kAttnCounterBytes);
+    p.part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kAttnCounterBytes +
                                          align_up(slots * kItemRows * kHD * sizeof(float), 256));
   }
   if (tc)  // one CTA = two work items
@@ -1239,7 +1309,7 @@ int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap&
   else
     attn_kernel<kVerify><<<dim3(grid_items, p.n_heads, p.kv_splits), kAttnThreads, kAttnSmem, stream>>>(mk, mv, p);
   if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
-  if (p.kv_splits > 1) {
+  if (!tc && p.kv_splits > 1) {  // the tcgen05 kernel merges its splits itself
     attn_combine_kernel<kVerify><<<dim3(grid_items, p.n_heads), 256, 0, stream>>>(p);
     if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
   }

@@ -73,15 +73,16 @@ def _sm_count(index: int) -> int:
 
 
 def auto_kv_splits(items: int, n_heads: int, max_keys: int, device: torch.device) -> int:
-    """Split each key range only for long key ranges on a grid that leaves
-    SMs idle.  The attention kernel runs one CTA per SM with two (item,
-    split) units per CTA; below ~1000 keys per unit a split's fixed cost (its
-    own prologue plus a combine pass) outweighs the parallelism it adds
-    (measured: 1 sequence x 896 keys is fastest unsplit)."""
+    """Key splits for the attention launch.  The kernel runs one CTA per SM
+    with two (item, split) units per CTA and merges a range's splits itself,
+    but that merge costs more than the parallelism buys at the cache lengths
+    measured so far (1 sequence x 896 keys: 24.6 us unsplit, 31-45 us with
+    2-7 splits), so ranges are split only when long (>= 4096 keys) on a grid
+    that leaves SMs idle."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     sms = _sm_count(idx)
     units = max(1, items * n_heads)
-    if units >= sms or max_keys < 2048:
+    if units >= sms or max_keys < 4096:
         return 1
     s = max(1, (2 * sms) // units)
     return min(s, max(1, max_keys // 1024), 16)
