@@ -154,12 +154,36 @@ def _time_kernels(model, n_rows, batch, lmax, dev):
     t_attn = timed(lambda: ops.attn_cache(q, att, kc, vc, plan, cap, scores, 1.0 / (bm * H), H, lmax,
                                           128 ** -0.5))
     t_norm = timed(lambda: ops.rmsnorm(x, blk.attn_norm.weight, 1e-5))
+    # Flash-Verify attention at the steady-state verify shape: per sequence 16
+    # drafts (2*bm rows: 32 trailing + 16 drafts twice), keys = the cache minus
+    # the block's own rows, the reference's verify mask
+    from flash_dllm_b200.generate import _verify_mask
+    s_d, t_d = 16, 2 * bm - 2 * 16
+    nd = lmax // 2
+    kparts, vrows, acc_k = [], [], 0
+    for j in range(batch):
+        kp = torch.cat([torch.arange(j * lmax, j * lmax + nd - t_d), torch.arange(j * lmax + nd + s_d, (j + 1) * lmax)])
+        kparts.append(kp)
+        vrows.append((acc_k, acc_k + kp.numel(), j * 2 * bm, (j + 1) * 2 * bm))
+        acc_k += kp.numel()
+    kpos = torch.cat(kparts).to(dev)
+    vblocks = torch.tensor(vrows, dtype=torch.int32, device=dev)
+    vmask = torch.from_numpy(np.concatenate([_verify_mask(bm, s_d)] * batch)).to(dev)
+    k1 = torch.randn(batch * 2 * bm, d, device=dev, generator=g).to(torch.bfloat16)
+    v1 = torch.randn_like(k1)
+    qv = torch.randn_like(k1)
+    ov = torch.empty_like(k1)
+    t_vattn = timed(lambda: ops.verify_attn(qv, k1, v1, ov, kc, vc, kpos, vmask, vblocks, 2 * bm, H, 128 ** -0.5,
+                                            max_keys=lmax))
     qkv_bytes = 3 * d * d * 2 + n_rows * d * 2 * 4 + n_rows * 8 + n_rows * 128 * 4 * 2
     qkv_flops = 2.0 * n_rows * d * 3 * d
     attn_bytes = batch * lmax * d * 2 * 2 + n_rows * d * 2 * 2 + batch * lmax * 4 * 2
     attn_flops = 4.0 * n_rows * lmax * d
-    return dict(qkv_s=t_qkv, attn_s=t_attn, norm_s=t_norm, qkv_bytes=qkv_bytes, qkv_flops=qkv_flops,
-                attn_bytes=attn_bytes, attn_flops=attn_flops, rows=n_rows)
+    # algorithmic bytes: every sequence's gathered cache K/V rows and its 2*bm own K/V rows read once, Q read
+    # and O written once
+    vattn_bytes = (acc_k + batch * 2 * bm) * d * 2 * 2 + batch * 2 * bm * d * 2 * 2
+    return dict(qkv_s=t_qkv, attn_s=t_attn, norm_s=t_norm, vattn_s=t_vattn, qkv_bytes=qkv_bytes, qkv_flops=qkv_flops,
+                attn_bytes=attn_bytes, attn_flops=attn_flops, vattn_bytes=vattn_bytes, rows=n_rows)
 
 
 def _cpu_reference(sample_layers: int = 1, vocab_slice: int = 8192):
@@ -389,6 +413,8 @@ def main():
             "tokens_timed": tok_all, "gpu_launches": launches * args.steps * world,
             "layer": {"qkv_us": kt["qkv_s"] * 1e6, "attn_us": kt["attn_s"] * 1e6, "rmsnorm_us": kt["norm_s"] * 1e6,
                       "attn_hbm_gbs": attn_gbs, "attn_frac_hbm": attn_gbs / hbm,
+                      "verify_attn_us": kt["vattn_s"] * 1e6,
+                      "verify_attn_frac_hbm": kt["vattn_bytes"] / kt["vattn_s"] / 1e9 / hbm,
                       "qkv_hbm_gbs": kt["qkv_bytes"] / kt["qkv_s"] / 1e9,
                       "qkv_tflops": kt["qkv_flops"] / kt["qkv_s"] / 1e12, "rows_per_gpu": rows},
             "roofline": roof,
