@@ -10,8 +10,10 @@ mask-view (acceptance prefix ``cumprod >= gamma``).
 
 What differs is how a step is executed.  Per-sequence host loops with
 ``.item()`` syncs become batched device kernels (fp64 confidence
-statistics, window acceptance, verify acceptance scan, refresh sort) with at
-most three small device->host reads per step; the LM head runs only on the
+statistics, window acceptance, verify acceptance scan, refresh sort) with
+one small device->host read per forward; the host keeps each sequence's
+query and key slots as index ranges into the device's slot order and sends
+one packed index array per forward; the LM head runs only on the
 rows the step reads (masked rows; verify mask-view rows); KV caches are
 zero-initialised.  Sorting ties resolve in index order (the reference's
 ``torch.sort`` is unstable).  Where the reference cannot continue -- a
@@ -156,7 +158,10 @@ def _session(model, B: int, L: int, head_dim: int, use_graphs: bool) -> _Session
 
 
 class _Slots:
-    """Host-side state of the sequence slots (the reference's per-slot lists)."""
+    """Host-side state of the sequence slots (the reference's per-slot lists).
+    The masked and tracked query sets are position ranges of the slot's row
+    of ``full_pos`` (the device-side slot order), gathered when a forward
+    runs."""
 
     def __init__(self, b: int):
         self.active = [-1] * b
@@ -164,8 +169,52 @@ class _Slots:
         self.pred = [0] * b
         self.eos = [-1] * b
         self.seqlen_k = [0] * b
-        self.masked = [None] * b
-        self.tracked = [None] * b
+        self.masked = [()] * b   # ((start, end),) positions of row j
+        self.tracked = [()] * b  # ((start, end), ...)
+
+
+def _multi_arange(starts, lens) -> np.ndarray:
+    """Concatenation of ``arange(starts[i], starts[i] + lens[i])`` (negative
+    lengths count as 0)."""
+    starts = np.asarray(starts, np.int64)
+    lens = np.maximum(np.asarray(lens, np.int64), 0)
+    total = int(lens.sum())
+    if total == 0:
+        return np.zeros(0, np.int64)
+    ends = np.cumsum(lens)
+    return np.arange(total, dtype=np.int64) + np.repeat(starts - (ends - lens), lens)
+
+
+def _ranges_idx(rows, L: int, ranges) -> np.ndarray:
+    """Flat ``full_pos`` indices of the position ranges of slot rows ``rows``
+    (``ranges[k]`` belongs to row ``rows[k]``), in order."""
+    st = [j * L + a for j, rs in zip(rows, ranges) for a, _ in rs]
+    ln = [b - a for rs in ranges for a, b in rs]
+    return _multi_arange(st, ln)
+
+
+def _count(ranges) -> int:
+    return sum(max(0, b - a) for a, b in ranges)
+
+
+class _Pack:
+    """Host arrays sent to the device in one pinned copy; ``views`` returns
+    the device tensors in the order they were added."""
+
+    def __init__(self):
+        self.parts = []
+
+    def add(self, a) -> None:
+        self.parts.append(np.ascontiguousarray(a, dtype=np.int64).reshape(-1))
+
+    def send(self, h2d):
+        sizes = [a.size for a in self.parts]
+        flat = h2d(torch.from_numpy(np.concatenate(self.parts) if self.parts else np.zeros(0, np.int64)))
+        out, o = [], 0
+        for n in sizes:
+            out.append(flat[o:o + n])
+            o += n
+        return out
 
 
 @torch.no_grad()
@@ -233,8 +282,8 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         st.pred[j] = p + gen_length + j * L
         st.eos[j] = -1
         st.seqlen_k[j] = (p + gen_length) // bn * bn + bn
-        st.masked[j] = full_pos[j, p:p + bm]
-        st.tracked[j] = torch.cat([full_pos[j, :p], full_pos[j, p + bm:st.seqlen_k[j]]])
+        st.masked[j] = ((p, p + bm),)
+        st.tracked[j] = ((0, p), (p + bm, max(st.seqlen_k[j], p + bm)))
         start_layer[j] = -1
 
     for j in range(B):
@@ -251,19 +300,37 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         m_rows, t_rows, acc = [], [], 0
         m_lens = []
         for j in act:
-            n = st.masked[j].numel()
+            n = _count(st.masked[j])
             m_lens.append(n)
             if n:
                 _tiles(m_rows, j, st.seqlen_k[j], acc, n, bm)
                 acc += n
         r_m = acc
         for j in act:
-            n = st.tracked[j].numel()
+            n = _count(st.tracked[j])
             if n:
                 _tiles(t_rows, j, st.seqlen_k[j], acc, n, bm)
                 acc += n
-        tables = h2d(torch.tensor(m_rows + t_rows, dtype=torch.int64).reshape(-1, 4))
-        query_pos_flat = torch.cat([st.masked[j] for j in act] + [st.tracked[j] for j in act])
+        na = len(act)
+        info = np.zeros((na, 4), np.int64)
+        off = 0
+        for k, j in enumerate(act):
+            info[k] = (off, m_lens[k], j * L + st.nd[j], st.pred[j])
+            off += m_lens[k]
+        pk = _Pack()
+        pk.add(np.array(m_rows + t_rows, np.int64))
+        pk.add(np.concatenate([_ranges_idx(act, L, [st.masked[j] for j in act]),
+                               _ranges_idx(act, L, [st.tracked[j] for j in act])]))
+        pk.add(info)
+        pk.add([1 if st.eos[j] != -1 else 0 for j in act])
+        pk.add(act)
+        pk.add([st.nd[j] for j in act])
+        pk.add([st.pred[j] for j in act])
+        tables, qidx, seq_info, eos_known, act_d, nd_d, pred_d = pk.send(h2d)
+        tables = tables.view(-1, 4)
+        seq_info = seq_info.view(-1, 4)
+        eos_known = eos_known.to(torch.int32)
+        query_pos_flat = full_pos.view(-1)[qidx]
         x_query = x[query_pos_flat]
         n_m = len(m_rows)
 
@@ -281,18 +348,14 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         if record is not None:
             record(False, x_query, query_pos_flat, None, logits, torch.arange(r_m, device=dev), attn_scores)
         p_max, x0, _ = ops.row_stats(logits)
-        info = np.zeros((len(act), 4), np.int64)
-        off = 0
-        for k, j in enumerate(act):
-            info[k] = (off, m_lens[k], j * L + st.nd[j], st.pred[j])
-            off += m_lens[k]
-        seq_info = h2d(torch.from_numpy(info))
-        eos_known = h2d(torch.tensor([1 if st.eos[j] != -1 else 0 for j in act], dtype=torch.int32))
         keep_d, len_d, eos_d = ops.window_accept(p_max, x0, query_pos_flat[:r_m], seq_info, eos_known, L, threshold,
                                                  min_keep, eos_id, full_pos, x, x_draft if verify else None)
-        host = d2h(torch.cat([keep_d.long(), len_d.long(), eos_d]))  # one device->host read
-        na = len(act)
-        keep1, lnum, eos1 = host[:na], host[na:2 * na], host[2 * na:]
+        parts = [keep_d.long(), len_d.long(), eos_d]
+        if not verify:
+            parts.append(_continues(full_pos, ar_L, act_d, nd_d, keep_d, pred_d, eos_known, eos_d))
+        host = d2h(torch.cat(parts))  # one device->host read
+        keep1, lnum, eos1 = host[:na], host[na:2 * na], host[2 * na:3 * na]
+        cont = host[3 * na:]
         for k, j in enumerate(act):
             st.nd[j] += keep1[k]
             if st.eos[j] == -1 and eos1[k] >= 0:
@@ -303,32 +366,44 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         # --------------------------------------------------- Flash-Verify --
         if verify:
             s_list = [min(max(lnum[k] - keep1[k], 0), bm // 2) for k in range(len(act))]
-            q_parts, k_parts, draft_parts, vrows, draft_flag, logit_idx = [], [], [], [], [], []
-            acc_q = acc_k = 0
-            for k, j in enumerate(act):
-                s = s_list[k]
-                t = 2 * bm - 2 * s
-                nd = st.nd[j]
-                tr = full_pos[j, nd - t:nd]
-                dr = full_pos[j, nd:nd + s]
-                q_parts += [tr, dr, dr]
-                k_parts += [full_pos[j, :nd - t], full_pos[j, nd + s:st.seqlen_k[j]]]
-                draft_parts.append(dr)
-                nq = tr.numel() + 2 * dr.numel()
-                nk = k_parts[-2].numel() + k_parts[-1].numel()
-                vrows.append((acc_k, acc_k + nk, acc_q, acc_q + nq))
-                draft_flag += [0] * tr.numel() + [1] * dr.numel() + [0] * dr.numel()
-                logit_idx += list(range(acc_q + tr.numel() + dr.numel(), acc_q + nq))
-                acc_q += nq
-                acc_k += nk
-            qpos = torch.cat(q_parts)
-            key_pos_flat = torch.cat(k_parts)
-            flag = h2d(torch.tensor(draft_flag, dtype=torch.bool))
-            x_verify = torch.where(flag, x_draft[qpos], x[qpos])
+            # every sequence has 2*bm verify rows: t trailing decoded slots, its
+            # s drafts, the same s slots again (mask view); keys are the rest
+            # of its cache range
+            s_a = np.array(s_list, np.int64)
+            t_a = 2 * bm - 2 * s_a
+            nd_a = np.array([st.nd[j] for j in act], np.int64)
+            sk_a = np.array([st.seqlen_k[j] for j in act], np.int64)
+            base = np.array(act, np.int64) * L + nd_a
+            P = np.arange(2 * bm, dtype=np.int64)[None, :]
+            T, S = t_a[:, None], s_a[:, None]
+            qi = (base[:, None] + np.where(P < T + S, P - T, P - T - S)).reshape(-1)
+            flags = ((P >= T) & (P < T + S)).reshape(-1)
+            di = qi[flags]
+            logit_idx = np.flatnonzero((P >= T + S).reshape(-1))
+            lens = np.stack([nd_a - t_a, sk_a - nd_a - s_a], 1)
+            ki = _multi_arange(np.stack([base - nd_a, base + s_a], 1).reshape(-1), lens.reshape(-1))
+            nk = np.maximum(lens, 0).sum(1)
+            k_end = np.cumsum(nk)
+            q0 = np.arange(len(act), dtype=np.int64) * 2 * bm
+            vrows = np.stack([k_end - nk, k_end, q0, q0 + 2 * bm], 1)
+            info2 = np.stack([np.cumsum(s_a) - s_a, s_a, np.zeros_like(s_a),
+                              np.array([st.pred[j] for j in act], np.int64)], 1)
+            pk = _Pack()
+            for part in (qi, ki, di, flags, logit_idx, vrows, info2):
+                pk.add(part)
+            pk.add([1 if st.eos[j] != -1 else 0 for j in act])
+            pk.add([st.nd[j] for j in act])
+            pk.add([st.pred[j] for j in act])
+            qi_d, ki_d, di_d, flag, lidx, vblocks, info2_d, eos_known, nd_d, pred_d = pk.send(h2d)
+            flat_pos = full_pos.view(-1)
+            qpos = flat_pos[qi_d]
+            key_pos_flat = flat_pos[ki_d]
+            draft_slots = flat_pos[di_d]
+            x_verify = torch.where(flag.bool(), x_draft[qpos], x[qpos])
             attn_mask = torch.cat([masks[s] for s in s_list])
-            vblocks = h2d(torch.tensor(vrows, dtype=torch.int32))
-            lidx = h2d(torch.tensor(logit_idx, dtype=torch.int64))
-            draft_slots = torch.cat(draft_parts) if draft_parts else empty_i64
+            vblocks = vblocks.view(-1, 4).to(torch.int32)
+            info2_d = info2_d.view(-1, 4)
+            eos_known = eos_known.to(torch.int32)
 
             def verify_forward(t, n_m=n_m):
                 positions = [t["qpos"], t["kpos"], rotary_emb_pos, [], attn_scores, t["mask"]]
@@ -351,16 +426,10 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                     record(True, x_verify, qpos, key_pos_flat, None, lidx, attn_scores)
                 draft_tok = draft_slots
                 p_tok = torch.zeros(0, dtype=torch.float64, device=dev)
-            info2 = np.zeros((len(act), 4), np.int64)
-            o2 = 0
-            for k, j in enumerate(act):
-                info2[k] = (o2, s_list[k], 0, st.pred[j])
-                o2 += s_list[k]
-            eos_known = h2d(torch.tensor([1 if st.eos[j] != -1 else 0 for j in act], dtype=torch.int32))
-            keep2_d, eos2_d = ops.verify_accept(p_tok, draft_tok, draft_slots, h2d(torch.from_numpy(info2)),
-                                                eos_known, gamma, eos_id, x)
-            host = d2h(torch.cat([keep2_d.long(), eos2_d]))
-            keep2, eos2 = host[:len(act)], host[len(act):]
+            keep2_d, eos2_d = ops.verify_accept(p_tok, draft_tok, draft_slots, info2_d, eos_known, gamma, eos_id, x)
+            cont_d = _continues(full_pos, ar_L, act_d, nd_d, keep2_d, pred_d, eos_known, eos2_d)
+            host = d2h(torch.cat([keep2_d.long(), eos2_d, cont_d]))
+            keep2, eos2, cont = host[:na], host[na:2 * na], host[2 * na:]
             for k, j in enumerate(act):
                 st.nd[j] += keep2[k]
                 if st.eos[j] == -1 and eos2[k] >= 0:
@@ -375,9 +444,6 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
             n_steps[st.active[j]] += 1
 
         # -------------------------------------------- refresh / finish --
-        ndp = h2d(torch.tensor([[st.nd[j] for j in act], [st.pred[j] for j in act], act], dtype=torch.int64))
-        rows = full_pos.index_select(0, ndp[2])
-        cont = d2h(((ar_L[None, :] >= ndp[0][:, None]) & (rows < ndp[1][:, None])).any(1))
         counts = np.zeros(B, np.int64)
         for k, j in enumerate(act):
             if cont[k]:
@@ -386,13 +452,15 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         for k, j in enumerate(act):
             nd = st.nd[j]
             if cont[k]:
-                st.masked[j] = full_pos[j, nd:nd + bm]
+                # full_pos only changes again in the next step's acceptance,
+                # after these ranges were gathered
+                st.masked[j] = ((nd, min(nd + bm, L)),)
                 if track_num < 0:
-                    st.tracked[j] = torch.cat([full_pos[j, :nd], full_pos[j, nd + bm:st.seqlen_k[j]]])
+                    st.tracked[j] = ((0, nd), (min(nd + bm, L), max(st.seqlen_k[j], min(nd + bm, L))))
                 else:
                     t0 = max(0, nd - track_num * bm)
                     t1 = min(st.seqlen_k[j], nd + bm * mask_num)
-                    st.tracked[j] = torch.cat([full_pos[j, t0:nd], full_pos[j, nd + bm:t1]])
+                    st.tracked[j] = ((t0, nd), (min(nd + bm, L), max(t1, min(nd + bm, L))))
                 start_layer[j] = n_layers
             else:
                 i = st.active[j]
@@ -413,8 +481,8 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                     count += 1
                 else:
                     st.active[j] = -1
-                    st.masked[j] = empty_i64
-                    st.tracked[j] = empty_i64
+                    st.masked[j] = ()
+                    st.tracked[j] = ()
         if trace is not None:
             rec["nd"] = list(st.nd)
             trace.append(rec)
@@ -426,6 +494,17 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         if max_steps is not None and step >= max_steps:
             break
     return responses, num_tokens, max_num_tokens
+
+
+def _continues(full_pos, ar_L, act_d, nd_d, keep_d, pred_d, eos_known, eos_d) -> torch.Tensor:
+    """Per active sequence (int64 0/1): does a slot before its predicted end
+    remain undecoded after this forward's acceptance?  ``nd_d``/``pred_d``
+    are the decoded count and predicted end before it; a newly found EOS
+    moves the end to just after it."""
+    nd = nd_d + keep_d.long()
+    pred = torch.where((eos_known == 0) & (eos_d >= 0), eos_d + 1, pred_d)
+    rows = full_pos.index_select(0, act_d)
+    return ((ar_L[None, :] >= nd[:, None]) & (rows < pred[:, None])).any(1).long()
 
 
 def _verify_mask(bm: int, s: int) -> np.ndarray:
