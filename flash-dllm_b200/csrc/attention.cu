@@ -85,7 +85,6 @@ struct AttnParams {
   float* scores;                // cache mode, optional
   float* part_o;                // split-KV partials [item][head][split][64][128]
   float* part_ml;               // [item][head][split][64][2]
-  int32_t* counters;            // tcgen05 kernel: splits done per (item, head), left at 0
   int32_t* status;
   int64_t n_slots;
   int64_t n_pos_k;
@@ -478,9 +477,13 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 // the block's own k1 / v1 rows under the verify mask).
 //
 // A kernel that uses tensor memory runs one CTA per SM, so each CTA runs two
-// independent pipelines ("halves"), each on its own (item, key split) unit --
-// units 2x and 2x+1 of the grid's x index, unit = item * kv_splits + split --
-// with its own shared memory, barriers and 256 TMEM columns.  A tcgen05.mma costs about the same issue time for any
+// independent pipelines ("halves"), each on its own work item -- items 2x and
+// 2x+1 for grid index x / kv_splits -- with its own shared memory, barriers
+// and 256 TMEM columns.  With kv_splits = S > 1 (S in {2, 4, 8}) the S CTAs
+// x = kv_splits * pair + s form a cluster, CTA s taking key slice s of both
+// items; each CTA leaves its unnormalised O rows and (m, l) in its own shared
+// memory and, after a cluster barrier, merges rows [64 s / S, 64 (s+1) / S)
+// of both items from all S CTAs through distributed shared memory.  A tcgen05.mma costs about the same issue time for any
 // M <= 128 and N <= 128, so each half issues few, wide ones: per 64-key tile
 // one M=128, N=64 S product (8 K-steps) and one M=128, N=128 PV product
 // (4 K-steps).  The 128 rows of a half's S operand are its 64 query rows and
@@ -565,6 +568,64 @@ __device__ __forceinline__ uint8_t* win_chunk(uint8_t* win, int row, int c) {
   return win + row * 128 + (((c & 7) ^ (row & 7)) << 4);
 }
 
+// Rows [64 s / S, 64 (s+1) / S) of one item, merged from the key slices of
+// the S CTAs of the cluster (CTA c's O rows at H.k, (m, l) at H.v, in its own
+// shared memory): O = sum_c 2^(m_c - m) O_c / sum_c 2^(m_c - m) l_c.  Thread
+// t of the half's 64 takes row 64 s / S + t / S and columns
+// (t % S) * 128 / S ... + 128 / S.
+template <int S>
+__device__ __forceinline__ void tc_merge_rows(const AttnParams& p, const TcHalf& H, const Item& it, int head,
+                                              int s, int t) {
+  constexpr int kCols = kHD / S;  // columns per thread
+  const int row = s * (kItemRows / S) + t / S;
+  const int part = t % S;
+  float m[S], w[S];
+  float mmax = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < S; ++c) {
+    const float2 ml = ld_dsmem_f2(mapa_shared(reinterpret_cast<const float2*>(H.v) + row, c));
+    m[c] = ml.x;
+    w[c] = ml.y;
+    mmax = fmaxf(mmax, ml.x);
+  }
+  const float ref = mmax == -INFINITY ? 0.f : mmax;
+  float lsum = 0.f;
+#pragma unroll
+  for (int c = 0; c < S; ++c) {
+    const float e = exp2f(m[c] - ref);
+    lsum += e * w[c];
+    w[c] = e;
+  }
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+  float acc[kCols];
+#pragma unroll
+  for (int j = 0; j < kCols; ++j) acc[j] = 0.f;
+  const uint8_t* orow = H.k + row * (kHD * 4);
+#pragma unroll
+  for (int c = 0; c < S; ++c) {
+#pragma unroll
+    for (int j = 0; j < kCols / 4; ++j) {
+      const int u = part * (kCols / 4) + j;
+      const float4 v = ld_dsmem_f4(mapa_shared(orow + ((u ^ (row & 7)) << 4), c));
+      acc[4 * j] += w[c] * v.x;
+      acc[4 * j + 1] += w[c] * v.y;
+      acc[4 * j + 2] += w[c] * v.z;
+      acc[4 * j + 3] += w[c] * v.w;
+    }
+  }
+  if (row >= it.rows) return;
+  __nv_bfloat16* dst = p.o + item_row(it, row) * p.d_model + head * kHD + part * kCols;
+#pragma unroll
+  for (int j = 0; j < kCols; j += 8) {
+    uint4 v;
+    v.x = pack_bf16x2(acc[j] * inv, acc[j + 1] * inv);
+    v.y = pack_bf16x2(acc[j + 2] * inv, acc[j + 3] * inv);
+    v.z = pack_bf16x2(acc[j + 4] * inv, acc[j + 5] * inv);
+    v.w = pack_bf16x2(acc[j + 6] * inv, acc[j + 7] * inv);
+    *reinterpret_cast<uint4*>(dst + j) = v;
+  }
+}
+
 template <bool kVerify>
 __global__ void __launch_bounds__(kTcThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
@@ -596,10 +657,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kH0Bar + 18 * 8);
   volatile int32_t* fail = reinterpret_cast<volatile int32_t*>(H.bar + 17);
 
-  // this half's work unit
-  const int unit = 2 * blockIdx.x + h;
-  const int item_id = unit / p.kv_splits;
-  const int split = unit % p.kv_splits;
+  // this half's work item and key split (split = rank in the cluster)
+  const int pair = blockIdx.x / p.kv_splits;
+  const int split = blockIdx.x % p.kv_splits;
+  const int item_id = 2 * pair + h;
   Item it{};
   const bool has_item = load_item(p, kVerify, item_id, it);
   // keys of this split: equal 64-aligned slices of the item's cache keys;
@@ -618,8 +679,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   {
     // the CTA exits only when neither half has an item
     Item other{};
-    const bool other_has = load_item(p, kVerify, (2 * blockIdx.x + (1 - h)) / p.kv_splits, other);
-    if (!has_item && !other_has) return;  // uniform across the CTA
+    const bool other_has = load_item(p, kVerify, 2 * pair + (1 - h), other);
+    if (!has_item && !other_has) return;  // uniform across the CTA and its cluster
   }
 
   if (role == kMma && lane == 0) {
@@ -655,7 +716,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int f = threadIdx.x >> 7, tid = threadIdx.x & 127;
     const TcHalf F = tc_half(smem, f);
     Item fi{};
-    const bool f_has = load_item(p, kVerify, (2 * blockIdx.x + f) / p.kv_splits, fi);
+    const bool f_has = load_item(p, kVerify, 2 * pair + f, fi);
     constexpr int kPer = kItemRows * 16 / 128;
     uint4 v[kPer];
 #pragma unroll
@@ -1026,12 +1087,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       } else {
-        // Split of a key range: store this split's unnormalised O row and
-        // (m, l); the last split of the (item, head) to finish merges them:
-        // O = sum_s 2^(m_s - m) O_s / sum_s 2^(m_s - m) l_s.
-        const int64_t pair = static_cast<int64_t>(item_id) * p.n_heads + head;
-        const int64_t slot0 = pair * p.kv_splits;
-        float* po = p.part_o + ((slot0 + split) * kItemRows + r) * kHD;
+        // Key slice of a cluster: this split's unnormalised O row (fp32,
+        // 16-byte units XOR-swizzled by row) goes to the half's K stages and
+        // (m, l) to its V stages -- both idle once the last PV product is done
+        uint8_t* orow = H.k + r * (kHD * 4);
 #pragma unroll 1
         for (int c = 0; c < kHD / 32; ++c) {
           float ov[32];
@@ -1042,70 +1101,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int j = 0; j < 32; ++j) ov[j] = 0.f;
           }
 #pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(po + 32 * c + j) = make_float4(ov[j], ov[j + 1], ov[j + 2], ov[j + 3]);
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(orow + (((c * 8 + j) ^ (r & 7)) << 4)) =
+                make_float4(ov[4 * j], ov[4 * j + 1], ov[4 * j + 2], ov[4 * j + 3]);
         }
-        *reinterpret_cast<float2*>(p.part_ml + ((slot0 + split) * kItemRows + r) * 2) =
-            make_float2(have_o ? m_used : -INFINITY, have_o ? l : 0.f);
-        __threadfence();
-        volatile int32_t* last_flag = reinterpret_cast<volatile int32_t*>(H.bar + 19);
-        if (h == 0)
-          asm volatile("bar.sync 3, 64;" ::: "memory");
-        else
-          asm volatile("bar.sync 4, 64;" ::: "memory");
-        if (r == 0) {
-          const int prev = atomicAdd(p.counters + pair, 1);
-          const int last = prev == p.kv_splits - 1 ? 1 : 0;
-          if (last) p.counters[pair] = 0;  // ready for the next call
-          *last_flag = last;
-          __threadfence();
-        }
-        if (h == 0)
-          asm volatile("bar.sync 3, 64;" ::: "memory");
-        else
-          asm volatile("bar.sync 4, 64;" ::: "memory");
-        if (*last_flag != 0 && row_ok) {
-          float mmax = -INFINITY;
-          for (int s2 = 0; s2 < p.kv_splits; ++s2)
-            mmax = fmaxf(mmax, __ldcg(p.part_ml + ((slot0 + s2) * kItemRows + r) * 2));
-          const float ref = mmax == -INFINITY ? 0.f : mmax;
-          float lsum = 0.f;
-          for (int s2 = 0; s2 < p.kv_splits; ++s2) {
-            const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + ((slot0 + s2) * kItemRows + r) * 2));
-            lsum += exp2f(ml.x - ref) * ml.y;
-          }
-          const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-          __nv_bfloat16* orow = p.o + grow * d + head * kHD;
-#pragma unroll 1
-          for (int c = 0; c < kHD / 32; ++c) {
-            float acc[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) acc[j] = 0.f;
-            for (int s2 = 0; s2 < p.kv_splits; ++s2) {
-              const float wgt = exp2f(__ldcg(p.part_ml + ((slot0 + s2) * kItemRows + r) * 2) - ref);
-              const float* src = p.part_o + ((slot0 + s2) * kItemRows + r) * kHD + 32 * c;
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src + j));
-                acc[j] += wgt * v4.x;
-                acc[j + 1] += wgt * v4.y;
-                acc[j + 2] += wgt * v4.z;
-                acc[j + 3] += wgt * v4.w;
-              }
-            }
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint4 v;
-              v.x = pack_bf16x2(acc[j] * inv, acc[j + 1] * inv);
-              v.y = pack_bf16x2(acc[j + 2] * inv, acc[j + 3] * inv);
-              v.z = pack_bf16x2(acc[j + 4] * inv, acc[j + 5] * inv);
-              v.w = pack_bf16x2(acc[j + 6] * inv, acc[j + 7] * inv);
-              *reinterpret_cast<uint4*>(orow + 32 * c + j) = v;
-            }
-          }
-        }
+        reinterpret_cast<float2*>(H.v)[r] = make_float2(have_o ? m_used : -INFINITY, have_o ? l : 0.f);
       }
     }
+  }
+
+  if (p.kv_splits > 1) {
+    // every thread of the cluster: the partials are in place ...
+    cluster_sync_all();
+    if (role == kSoftmax && has_item) {
+      const int t = (warp & 1) * 32 + lane;
+      if (p.kv_splits == 2)
+        tc_merge_rows<2>(p, H, it, head, split, t);
+      else if (p.kv_splits == 4)
+        tc_merge_rows<4>(p, H, it, head, split, t);
+      else
+        tc_merge_rows<8>(p, H, it, head, split, t);
+    }
+    // ... and stay readable until every CTA of the cluster has merged
+    cluster_sync_all();
   }
 
   tc_fence_before();
@@ -1252,17 +1270,18 @@ namespace {
 
 int plan_capacity(int32_t n_rows, int32_t batch) { return (n_rows + kItemRows - 1) / kItemRows + batch; }
 
-// Workspace layout when keys are split: a fixed counter region (one counter
-// per (item, head), left at zero after every call, at the same place for
-// every call), then the partial O rows, then the partial (m, l).
-constexpr size_t kAttnCounterBytes = 64 * 1024;
-
+// Workspace layout when keys are split (mma.sync kernel: its combine kernel
+// reads them; the tcgen05 kernel merges in distributed shared memory): the
+// partial O rows, then the partial (m, l).
 size_t attn_ws_bytes(int32_t items, int32_t heads, int32_t splits) {
   if (splits <= 1) return 256;
   const size_t slots = static_cast<size_t>(items) * heads * splits;
-  return kAttnCounterBytes + align_up(slots * kItemRows * kHD * sizeof(float), 256) +
-         slots * kItemRows * 2 * sizeof(float);
+  return align_up(slots * kItemRows * kHD * sizeof(float), 256) + slots * kItemRows * 2 * sizeof(float);
 }
+
+// Key splits the tcgen05 kernel runs: its cluster merge takes 1, 2, 4 or 8
+// (a request in between rounds down; results do not depend on the split).
+int tc_splits(int requested) { return requested >= 8 ? 8 : requested >= 4 ? 4 : requested >= 2 ? 2 : 1; }
 
 // Attention runs on the tcgen05 kernel; FDLLM_ATTN_MMA_SYNC=1 selects the
 // mma.sync kernel instead (kept as the comparison point).
@@ -1293,23 +1312,39 @@ int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap&
       return FDLLM_ERR_CUDA;
     attr[dev] = true;
   }
+  if (tc) {
+    // one CTA = two work items; key splits as clusters of CTAs
+    p.kv_splits = tc_splits(p.kv_splits);
+    const dim3 grid(static_cast<unsigned>((grid_items + 1) / 2 * p.kv_splits), static_cast<unsigned>(p.n_heads), 1);
+    if (p.kv_splits == 1) {
+      attn_tc_kernel<kVerify><<<grid, kTcThreads, kTcSmem, stream>>>(mk, mv, mk1, mv1, p);
+    } else {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = grid;
+      cfg.blockDim = dim3(kTcThreads, 1, 1);
+      cfg.dynamicSmemBytes = kTcSmem;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr_c[1];
+      attr_c[0].id = cudaLaunchAttributeClusterDimension;
+      attr_c[0].val.clusterDim.x = static_cast<unsigned>(p.kv_splits);
+      attr_c[0].val.clusterDim.y = 1;
+      attr_c[0].val.clusterDim.z = 1;
+      cfg.attrs = attr_c;
+      cfg.numAttrs = 1;
+      if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<kVerify>, mk, mv, mk1, mv1, p) != cudaSuccess)
+        return FDLLM_ERR_CUDA;
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
+  }
   if (p.kv_splits > 1) {
     if (ws == nullptr || ws_bytes < attn_ws_bytes(grid_items, p.n_heads, p.kv_splits)) return FDLLM_ERR_WORKSPACE;
-    if (static_cast<size_t>(grid_items) * p.n_heads * sizeof(int32_t) > kAttnCounterBytes) return FDLLM_ERR_ARG;
     const size_t slots = static_cast<size_t>(grid_items) * p.n_heads * p.kv_splits;
-    p.counters = static_cast<int32_t*>(ws);
-    p.part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kAttnCounterBytes);
-    p.part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kAttnCounterBytes +
-                                         align_up(slots * kItemRows * kHD * sizeof(float), 256));
+    p.part_o = static_cast<float*>(ws);
+    p.part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align_up(slots * kItemRows * kHD * sizeof(float), 256));
   }
-  if (tc)  // one CTA = two work items
-    attn_tc_kernel<kVerify>  // one CTA = two (item, split) units
-        <<<dim3((grid_items * p.kv_splits + 1) / 2, p.n_heads, 1), kTcThreads, kTcSmem, stream>>>(mk, mv, mk1, mv1,
-                                                                                                  p);
-  else
-    attn_kernel<kVerify><<<dim3(grid_items, p.n_heads, p.kv_splits), kAttnThreads, kAttnSmem, stream>>>(mk, mv, p);
+  attn_kernel<kVerify><<<dim3(grid_items, p.n_heads, p.kv_splits), kAttnThreads, kAttnSmem, stream>>>(mk, mv, p);
   if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
-  if (!tc && p.kv_splits > 1) {  // the tcgen05 kernel merges its splits itself
+  if (p.kv_splits > 1) {
     attn_combine_kernel<kVerify><<<dim3(grid_items, p.n_heads), 256, 0, stream>>>(p);
     if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
   }

@@ -74,18 +74,17 @@ def _sm_count(index: int) -> int:
 
 def auto_kv_splits(items: int, n_heads: int, max_keys: int, device: torch.device) -> int:
     """Key splits for the attention launch.  The kernel runs one CTA per SM
-    with two (item, split) units per CTA and merges a range's splits itself,
-    but that merge costs more than the parallelism buys at the cache lengths
-    measured so far (1 sequence x 896 keys: 24.6 us unsplit, 31-45 us with
-    2-7 splits), so ranges are split only when long (>= 4096 keys) on a grid
-    that leaves SMs idle."""
+    with two work items per CTA; a split count S (1, 2, 4 or 8) runs each
+    pair of items on a cluster of S CTAs, one key slice each, merged in
+    distributed shared memory.  Split only while the grid still fits one wave
+    and every slice keeps at least two 64-key tiles."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     sms = _sm_count(idx)
-    units = max(1, items * n_heads)
-    if units >= sms or max_keys < 4096:
-        return 1
-    s = max(1, (2 * sms) // units)
-    return min(s, max(1, max_keys // 1024), 16)
+    ctas = max(1, (items + 1) // 2) * n_heads
+    s = 1
+    while s < 8 and 2 * s * ctas <= sms and max_keys // (2 * s) >= 128:
+        s *= 2
+    return s
 
 
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:

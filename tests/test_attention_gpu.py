@@ -84,7 +84,7 @@ def test_cache_attention_golden_case():
     assert _rel(sc, so) <= SCORE_TOL
 
 
-@pytest.mark.parametrize("kv_splits", [0, 1, 3])
+@pytest.mark.parametrize("kv_splits", [0, 1, 3, 8])  # 3 runs as 2 (cluster merge: 1, 2, 4, 8)
 def test_cache_attention_config2_shape(kv_splits):
     """BASELINE config 2 shape: 8 sequences, k_end uniform in [256,1024] step
     32, 32 masked rows + 0..32 refresh rows each, 32 heads x 128."""
@@ -203,7 +203,7 @@ def test_verify_attention_golden_case():
     _check_verify(v, cases.BLOCK_M, cases.N_HEADS)
 
 
-@pytest.mark.parametrize("kv_splits", [0, 1, 4])
+@pytest.mark.parametrize("kv_splits", [0, 1, 4, 8])
 def test_verify_attention_config4_shape(kv_splits):
     """bm 32 -> 64 verify rows per sequence, 8 sequences, 32 heads, ~830
     gathered cache keys each, varied draft counts S (0..16)."""
