@@ -796,10 +796,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int pending = -1;  // gathered tile not yet published
     for (int t = 0; t < n_tiles; ++t) {
       const int s = t & 1;
-      if (t >= 2 && !mbar_wait(&empty[s], ((t - 2) >> 1) & 1, p.status, kAttnKernelId)) {
-        ok = false;
-        break;
-      }
+      // the tile's key rows are read before waiting for its stage, so the
+      // position loads overlap the wait
       const bool blk = t >= nt_cache;
       const int n0 = blk ? (t - nt_cache) * kKeyTile : c0 + t * kKeyTile;
       const int n_end = blk ? it.blk_rows : c1;
@@ -814,13 +812,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           } else {
             const int64_t pk = static_cast<int64_t>(it.k_base) + n;
             row = (pk < p.n_pos_k) ? p.pos_k[pk] : -1;
-            if (row < 0 || row >= p.n_slots) {
-              if (is_k) report(p.status, FDLLM_ERR_INDEX, static_cast<int>(pk), kAttnKernelId);
-              row = -1;
-            }
           }
         }
         src_row[hh] = row;
+      }
+      if (t >= 2 && !mbar_wait(&empty[s], ((t - 2) >> 1) & 1, p.status, kAttnKernelId)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int n = n0 + lane + 32 * hh;
+        if (!blk && n < n_end && (src_row[hh] < 0 || src_row[hh] >= p.n_slots)) {
+          if (is_k) report(p.status, FDLLM_ERR_INDEX, static_cast<int>(it.k_base + n), kAttnKernelId);
+          src_row[hh] = -1;
+        }
       }
       uint8_t* dst = (is_k ? H.k : H.v) + s * kTileBytes;
       const int64_t row0 = __shfl_sync(0xffffffffu, src_row[0], 0);
