@@ -359,10 +359,12 @@ struct QkvPlan {
   int grid;
 };
 
-// Units are spread round-robin over one CTA per SM.  A K split is used only
-// when there are fewer tiles than SMs; the split count maximises the balance
-// units / (ceil(units / SMs) * SMs), preferring fewer splits, with at least 8
-// k-blocks per split.
+// Units are spread round-robin over one CTA per SM.  Tiles are 128 columns
+// (one head) wide and K is not split by default: at 64 and 128 rows (96
+// tiles) whole-K tiles on 96 SMs measured faster than 64-wide tiles on all
+// SMs (64 rows: 35.5 vs 39.6 us) and than 2-6 K splits, whose fp32 partials
+// cost more than the balance gains (64 rows: 41.7-92 us).  FDLLM_QKV_BN /
+// FDLLM_QKV_SPLITS / FDLLM_QKV_KSUB override the choices.
 QkvPlan plan_qkv(int32_t n_rows, int32_t d_model, int32_t n_heads) {
   QkvPlan pl{};
   int ksub = env_int("FDLLM_QKV_KSUB", 0);
@@ -374,26 +376,11 @@ QkvPlan plan_qkv(int32_t n_rows, int32_t d_model, int32_t n_heads) {
   pl.m_tiles = (n_rows + kQkvBM - 1) / kQkvBM;
   pl.xrows = n_rows <= 64 ? 64 : 128;
   int bn = env_int("FDLLM_QKV_BN", 0);
-  if (bn != 64 && bn != 128) bn = n_rows <= 64 ? 64 : 128;  // measured best at 64 / 512 rows
+  if (bn != 64 && bn != 128) bn = 128;
   pl.bn = bn;
   pl.n_tiles = 3 * n_heads * (128 / bn);
   const int tiles = pl.m_tiles * pl.n_tiles;
-  int splits = env_int("FDLLM_QKV_SPLITS", 0);
-  if (splits <= 0) {
-    splits = 1;
-    if (tiles < sms) {
-      double best = 0.0;
-      for (int s = 1; s <= 16 && kb_total / s >= 8 / ksub; ++s) {
-        const int units = tiles * s;
-        const int waves = (units + sms - 1) / sms;
-        const double bal = static_cast<double>(units) / (static_cast<double>(waves) * sms);
-        if (bal > best + 0.02) {
-          best = bal;
-          splits = s;
-        }
-      }
-    }
-  }
+  int splits = env_int("FDLLM_QKV_SPLITS", 1);
   if (splits < 1) splits = 1;
   if (splits > kb_total) splits = kb_total;
   pl.kb_per_split = (kb_total + splits - 1) / splits;
@@ -406,7 +393,7 @@ QkvPlan plan_qkv(int32_t n_rows, int32_t d_model, int32_t n_heads) {
 // Workspace layout: a fixed counter region (so counters never move between
 // calls with different tile counts, and no call's partial sums land on another
 // call's counters), then the split-K partials.
-constexpr size_t kQkvCounterBytes = 4096;  // 1024 tiles; a K split is only used below the SM count
+constexpr size_t kQkvCounterBytes = 4096;  // 1024 tiles (K splits are requested through FDLLM_QKV_SPLITS)
 
 size_t qkv_ws_bytes(const QkvPlan& pl) {
   if (pl.splits <= 1) return 256;

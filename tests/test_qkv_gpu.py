@@ -44,7 +44,8 @@ def _oracle(x, w, pos, kc, vc, sin, cos, n_heads):
 
 
 @pytest.mark.parametrize("n_rows,d_model,n_slots,env", [
-    (64, 4096, 512, {}),                                     # BASELINE config 1 shape (split-K)
+    (64, 4096, 512, {}),                                     # BASELINE config 1 shape
+    (64, 4096, 512, {"FDLLM_QKV_SPLITS": "3"}),              # the same with split-K
     (64, 4096, 512, {"FDLLM_QKV_BN": "64", "FDLLM_QKV_SPLITS": "1"}),
     (1, 256, 64, {}),
     (59, 256, 256, {"FDLLM_QKV_SPLITS": "2"}),

@@ -44,10 +44,11 @@ def _noalloc(lib, x, w, pos, sin, cos, q, kc, vc, n_heads):
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
 
 
-def test_noalloc_matches_workspace_entry_point_twice():
+def test_noalloc_matches_workspace_entry_point_twice(monkeypatch):
     import flash_dllm_b200.ops as ops
     from flash_dllm_b200._lib import check_device_status, lib
-    n_rows, d_model, n_slots = 64, 4096, 512   # split-K, uses the scratch
+    monkeypatch.setenv("FDLLM_QKV_SPLITS", "3")  # split-K: the partial sums use the scratch
+    n_rows, d_model, n_slots = 64, 4096, 512   # BASELINE config 1 shape
     n_heads = d_model // 128
     x, w, pos, kc0, vc0, sin, cos = _inputs(n_rows, d_model, n_slots, seed=11)
     q_ref = torch.empty_like(x)
