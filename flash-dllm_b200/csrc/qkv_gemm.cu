@@ -345,6 +345,486 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant (more than 128 rows).  A cluster of two CTAs computes
+// 256-row x 256-column tiles (two heads; the last tile of an odd head count
+// is one head) with 2-SM UMMAs (cta_group::2, M = 256): CTA r loads rows
+// 128r..128r+127 of the tile's X rows and head h0 + r of its W rows (rows
+// 64r..64r+63 of a one-head tile), and holds its 128 output rows in its own
+// TMEM.  Each SM then moves 512 operand bytes per 64K flops of a k-step,
+// which keeps it under the ~108 GB/s an SM pulls from L2 through TMA.
+//
+// Work is split stream-K: the (tile, k-block) iterations are cut into one
+// contiguous range per pair.  A range that starts inside a tile contributes
+// that tile's last k-blocks first and stores the partial accumulator (fp32,
+// one slot per pair) with a release flag; the pair whose range holds the
+// tile's k-block 0 does that tile last, adds the partials of the pairs after
+// it and runs the epilogue.  Owners only wait on pairs of higher index that
+// did their part first, on a grid that is resident all at once.
+//
+// Rank 0 issues the MMAs; the leader's `full` barrier expects the bytes of
+// both CTAs' loads, which complete their transactions on it (plain loads, no
+// multicast); stage and accumulator completions are committed to both CTAs.
+// Warpgroup 0 holds the TMA producer and MMA warps and gives registers up
+// (setmaxnreg 48) to warpgroups 1-2, the eight epilogue warps (224 each, two
+// per TMEM lane quarter), which move each 32-column slice
+// and its RoPE partner slice 64 columns on from TMEM through a swizzled fp32
+// staging buffer, so that the RoPE tables are read and the outputs written
+// row-contiguously, sixteen rows per warp in one batch of loads.  The last
+// segment's epilogue is not hidden behind MMAs: it first copies the RoPE
+// rows of its 128 rows into the (then idle) operand ring with cp.async and
+// reads them from there.
+// ---------------------------------------------------------------------------
+constexpr int kQ2ABytes = kQkvBM * kQkvBK * 2;                // 128 X rows x 64 K
+constexpr int kQ2BHalfBytes = 64 * kQkvBK * 2;                // 64 W rows x 64 K
+constexpr int kQ2StageBytes = kQ2ABytes + 2 * kQ2BHalfBytes;  // 32 KB
+constexpr int kQ2Stages = 6;
+constexpr int kQ2StagingOffset = kQ2Stages * kQ2StageBytes;
+constexpr int kQ2StagingBytes = kQkvBM * 64 * 4;  // 128 rows x (32 + 32) fp32
+constexpr int kQ2BarOffset = kQ2StagingOffset + kQ2StagingBytes;
+constexpr int kQ2Smem = 1024 + kQ2BarOffset + 256;
+constexpr int kQ2AccCols = 256;
+constexpr int kQ2TmemCols = 2 * kQ2AccCols;          // double-buffered accumulator
+constexpr int kQ2PartialFloats = kQkvBM * kQ2AccCols;  // one CTA's partial accumulator
+constexpr int kQ2Threads = 384;  // warpgroup 0: producer, MMA, 2 idle; warpgroups 1-2: epilogue
+// Register split: 128 x 48 + 256 x 224 <= 384 x 168 at launch.
+constexpr int kQ2RegsLow = 48, kQ2RegsHigh = 224;
+static_assert(128 * kQ2RegsLow + 256 * kQ2RegsHigh <= kQ2Threads * 168, "setmaxnreg split");
+static_assert(kQ2Smem <= 232448, "CTA-pair QKV shared memory");
+
+struct Q2Seg {
+  int tile, k0, k1;  // k-blocks [k0, k1) of `tile`
+};
+
+__device__ __forceinline__ int q2_lo(int pair, int n_pairs, int iters) {
+  return static_cast<int>(static_cast<long long>(pair) * iters / n_pairs);
+}
+
+// Next segment of the iteration range [i, hi): the k-blocks of one tile.
+__device__ __forceinline__ bool q2_next(int& i, int hi, int kbt, Q2Seg& s) {
+  if (i >= hi) return false;
+  s.tile = i / kbt;
+  s.k0 = i % kbt;
+  s.k1 = s.k0 + (hi - i) < kbt ? s.k0 + (hi - i) : kbt;
+  i += s.k1 - s.k0;
+  return true;
+}
+
+// RoPE + bf16 store of 16 staged rows of one 32-column slice (and its
+// partners 64 columns on): half-warp hw of the warp takes rows 2k + hw of its
+// 16, lane j the columns c, c + 1, with the RoPE rows read from the tables by
+// slot and the outputs written to `out` (head column 0) by row or slot.  Rows
+// whose slot is negative are not written.
+__device__ __forceinline__ void q2_rope_rows(const float* staging, const QkvParams& p, int quarter, int half, int hw,
+                                             int j, int c, bool rope, int64_t my_slot, __nv_bfloat16* out, int d,
+                                             bool by_slot, int row_base) {
+  float2 y1[8], y2[8];
+  int64_t sl[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int rr = half * 16 + 2 * k + hw;  // row within the warp's quarter
+    const int rt = quarter * 32 + rr;
+    sl[k] = __shfl_sync(0xffffffffu, my_slot, rr);
+    const float* st = staging + rt * 64;
+    const int pu = (j >> 1) ^ (rt & 7);
+    const float2 x1 = *reinterpret_cast<const float2*>(st + pu * 4 + (j & 1) * 2);
+    const float2 x2 = *reinterpret_cast<const float2*>(st + 32 + pu * 4 + (j & 1) * 2);
+    y1[k] = x1;
+    y2[k] = x2;
+    if (rope) {
+      const int64_t sr = sl[k] < 0 ? 0 : sl[k];  // invalid rows read slot 0 and are not stored
+      const float2 s1 = __ldg(reinterpret_cast<const float2*>(p.sin + sr * 128 + c));
+      const float2 s2 = __ldg(reinterpret_cast<const float2*>(p.sin + sr * 128 + c + 64));
+      const float2 c1 = __ldg(reinterpret_cast<const float2*>(p.cos + sr * 128 + c));
+      const float2 c2 = __ldg(reinterpret_cast<const float2*>(p.cos + sr * 128 + c + 64));
+      y1[k].x = x1.x * c1.x - x2.x * s1.x;
+      y1[k].y = x1.y * c1.y - x2.y * s1.y;
+      y2[k].x = x2.x * c2.x + x1.x * s2.x;
+      y2[k].y = x2.y * c2.y + x1.y * s2.y;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int rt = quarter * 32 + half * 16 + 2 * k + hw;
+    if (sl[k] >= 0) {
+      const int64_t orow = by_slot ? sl[k] : static_cast<int64_t>(row_base + rt);
+      __nv_bfloat16* dst = out + orow * d;
+      *reinterpret_cast<uint32_t*>(dst + c) = pack_bf16x2(y1[k].x, y1[k].y);
+      *reinterpret_cast<uint32_t*>(dst + c + 64) = pack_bf16x2(y2[k].x, y2[k].y);
+    }
+  }
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kQ2Threads, 1)
+    qkv2_rope_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_wq,
+                     const __grid_constant__ CUtensorMap map_wk, const __grid_constant__ CUtensorMap map_wv,
+                     const QkvParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* staging = reinterpret_cast<float*>(smem + kQ2StagingOffset);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kQ2BarOffset);
+  uint64_t* empty = full + kQ2Stages;
+  uint64_t* acc_full = empty + kQ2Stages;  // [2] MMA -> epilogue (both CTAs)
+  uint64_t* acc_empty = acc_full + 2;      // [2] epilogues of both CTAs -> MMA (leader's)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int32_t* abort_flag = reinterpret_cast<int32_t*>(tmem_slot + 1);
+  uint64_t* tab_bar = acc_empty + 3;  // last segment: RoPE rows landed (256 arrivals)
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair_id = blockIdx.x >> 1;
+  const int n_pairs = gridDim.x >> 1;
+  const int m_pairs = (p.n_rows + 2 * kQkvBM - 1) / (2 * kQkvBM);
+  const int n_blocks = 3 * p.n_heads;
+  const int kbt = p.d_model / kQkvBK;
+  const int iters = m_pairs * ((n_blocks + 1) / 2) * kbt;
+  const int lo = q2_lo(pair_id, n_pairs, iters);
+  const int hi = q2_lo(pair_id + 1, n_pairs, iters);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kQ2Stages; ++s) {
+      mbar_init(&full[s], 1);   // the leader's expect_tx arrival (used on the leader)
+      mbar_init(&empty[s], 1);  // the leader's commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 16);  // 8 epilogue warps x 2 CTAs (used on the leader)
+    }
+    mbar_init(tab_bar, 256);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_x);
+    tma_prefetch_desc(&map_wq);
+    tma_prefetch_desc(&map_wk);
+    tma_prefetch_desc(&map_wv);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, kQ2TmemCols);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kQ2RegsLow));
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer --
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      int i = lo;
+      Q2Seg sg;
+      while (ok && q2_next(i, hi, kbt, sg)) {
+        const int m_pair = sg.tile % m_pairs, b = (sg.tile / m_pairs) * 2;
+        const int nblk = n_blocks - b < 2 ? n_blocks - b : 2;
+        // W rows this CTA loads: head b + rank (two heads) or half `rank` of head b
+        const int head_g = nblk == 2 ? b + static_cast<int>(rank) : b;
+        const int proj = head_g / p.n_heads;
+        const int w_row = (head_g % p.n_heads) * 128 + (nblk == 2 ? 0 : static_cast<int>(rank) * 64);
+        const CUtensorMap* map_w = proj == 0 ? &map_wq : (proj == 1 ? &map_wk : &map_wv);
+        const uint32_t tx = 2u * static_cast<uint32_t>(kQ2ABytes + nblk * kQ2BHalfBytes);
+        const int x_row = m_pair * 2 * kQkvBM + static_cast<int>(rank) * kQkvBM;
+        for (int kb = sg.k0; kb < sg.k1; ++kb, ++g) {
+          const int s = g % kQ2Stages;
+          const uint32_t ph = (g / kQ2Stages) & 1;
+          if (g >= static_cast<uint32_t>(kQ2Stages) && !mbar_wait(&empty[s], ph ^ 1, p.status, kQkvKernelId)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a = smem + s * kQ2StageBytes;
+          const uint32_t bar = mapa_shared(&full[s], 0);
+          // the leader expects both CTAs' bytes; the peer's loads only
+          // complete transactions on it (a cluster-scope arrive per stage
+          // costs about one load latency, serialising the ring)
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], tx);
+          tma_load_2d_pair(a, &map_x, kb * kQkvBK, x_row, bar);
+          tma_load_2d_pair(a + kQ2ABytes, map_w, kb * kQkvBK, w_row, bar);
+          if (nblk == 2) tma_load_2d_pair(a + kQ2ABytes + kQ2BHalfBytes, map_w, kb * kQkvBK, w_row + 64, bar);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------- MMA issuer (leader only) --
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc1 = umma_idesc_bf16(2 * kQkvBM, 128);
+      constexpr uint32_t idesc2 = umma_idesc_bf16(2 * kQkvBM, 256);
+      uint32_t g = 0;
+      int i_unit = 0;
+      bool ok = true;
+      int i = lo;
+      Q2Seg sg;
+      while (ok && q2_next(i, hi, kbt, sg)) {
+        const int b = (sg.tile / m_pairs) * 2;
+        const uint32_t idesc = n_blocks - b < 2 ? idesc1 : idesc2;
+        const int acc = i_unit & 1;
+        if (i_unit >= 2 && !mbar_wait(&acc_empty[acc], ((i_unit >> 1) & 1) ^ 1, p.status, kQkvKernelId)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kQ2AccCols;
+        for (int kb = sg.k0; kb < sg.k1; ++kb, ++g) {
+          const int s = g % kQ2Stages;
+          const uint32_t ph = (g / kQ2Stages) & 1;
+          if (!mbar_wait(&full[s], ph, p.status, kQkvKernelId)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* a = smem + s * kQ2StageBytes;
+          const uint64_t da = umma_desc_kmajor_sw128(smem_u32(a));
+          const uint64_t db = umma_desc_kmajor_sw128(smem_u32(a + kQ2ABytes));
+#pragma unroll
+          for (int k = 0; k < kQkvBK / 16; ++k)
+            umma_bf16_pair(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb > sg.k0 || k > 0) ? 1u : 0u);
+          umma_commit_pair(mapa_shared(&empty[s], 0));
+          umma_commit_pair(mapa_shared(&empty[s], 1));
+        }
+        if (!ok) break;
+        umma_commit_pair(mapa_shared(&acc_full[acc], 0));
+        umma_commit_pair(mapa_shared(&acc_full[acc], 1));
+        ++i_unit;
+      }
+    }
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kQ2RegsHigh));
+    // ---------------------------------------------------------- epilogue --
+    const int quarter = warp & 3;
+    const int half = (warp - 4) >> 2;        // 0: a-columns / first 16 rows, 1: partner columns / last 16
+    const int r_tile = quarter * 32 + lane;  // this thread's TMEM lane / tile row
+    const int ep_tid = threadIdx.x - 128;
+    const int d = p.d_model;
+    int i_unit = 0;
+    int i = lo;
+    Q2Seg sg;
+    while (q2_next(i, hi, kbt, sg)) {
+      const bool last = i >= hi;
+      const int m_pair = sg.tile % m_pairs, b = (sg.tile / m_pairs) * 2;
+      const int nblk = n_blocks - b < 2 ? n_blocks - b : 2;
+      const int acc = i_unit & 1;
+      const uint32_t t_base = tmem_base + acc * kQ2AccCols + (static_cast<uint32_t>(quarter * 32) << 16);
+      // row slot, and its RoPE rows pulled into L2 while the MMAs run (the
+      // epilogue's table reads are otherwise serialised DRAM round trips)
+      const int row_base = m_pair * 2 * kQkvBM + static_cast<int>(rank) * kQkvBM;
+      int64_t my_slot = -1;  // slot of row r_tile; -1: row not written
+      if (sg.k0 == 0 && row_base + r_tile < p.n_rows) {
+        const int64_t s = p.pos[row_base + r_tile];
+        if (s < 0 || s >= p.n_slots) {
+          report(p.status, FDLLM_ERR_INDEX, row_base + r_tile, kQkvKernelId);
+        } else {
+          my_slot = s;
+          if (b / p.n_heads < 2) {
+            const float* tab = half == 0 ? p.sin : p.cos;
+#pragma unroll
+            for (int l = 0; l < 128; l += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(tab + s * 128 + l));
+          }
+        }
+      }
+      if (!mbar_wait(&acc_full[acc], (i_unit >> 1) & 1, p.status, kQkvKernelId)) *abort_flag = 1;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (*abort_flag != 0) break;
+      tc_fence_after();
+      ++i_unit;
+      if (sg.k0 > 0) {
+        // contributor: store the partial sums ([col / 4][row][4] fp32, so a
+        // warp's accesses are 512 contiguous bytes) and publish them
+        float4* part = reinterpret_cast<float4*>(p.partials) + static_cast<size_t>(pair_id * 2 + rank) *
+                                                                  (kQ2PartialFloats / 4);
+        for (int c = half * 32; c < nblk * 128; c += 64) {
+          float v[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(t_base + c, v);
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            __stcg(part + ((c + j) >> 2) * kQkvBM + r_tile, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+        __threadfence();
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (ep_tid == 0) st_release_gpu(p.counters + pair_id * 2 + rank, 1);
+        continue;
+      }
+      // a whole tile, or the owner's part (k-block 0 on): add the partials of
+      // the pairs whose ranges start inside this tile
+      int q_end = pair_id + 1;
+      if (sg.k1 < kbt) {
+        const int t_end = (sg.tile + 1) * kbt;
+        while (q_end < n_pairs && q2_lo(q_end, n_pairs, iters) < t_end) ++q_end;
+        for (int q = pair_id + 1; q < q_end; ++q) flag_wait_set(p.counters + q * 2 + rank, p.status, kQkvKernelId);
+      }
+      const bool rope_tile = b / p.n_heads < 2;  // the tile has a Q or K head
+      if (last) {
+        // The last segment's epilogue is not hidden behind MMAs, and the ring
+        // is idle then (every MMA that read it has completed).  It runs
+        // thread-per-row straight from TMEM: the rows' RoPE tables are
+        // bulk-copied into the ring with a 1040-byte row stride (a warp's
+        // 16-byte reads of 32 rows then spread over all bank groups), the
+        // contributor's partial sums (if any) come by coalesced loads, and
+        // the bf16 rows are staged (272-byte stride) and leave by one 256-byte
+        // bulk store per row and head.  Half h takes head columns 32h..32h+31
+        // and their partners 64 + 32h.. of every head.
+        constexpr int kTabStride = 1040, kOutStride = 272;
+        uint8_t* tabs = smem;                        // row r: sin[128] | cos[128] fp32
+        uint8_t* outs = smem + kQkvBM * kTabStride;  // head hh, row r: 128 bf16
+        if (rope_tile) {
+          mbar_arrive_expect_tx(tab_bar, my_slot >= 0 ? 512u : 0u);
+          if (my_slot >= 0)
+            bulk_load(tabs + r_tile * kTabStride + half * 512, (half == 0 ? p.sin : p.cos) + my_slot * 128, 512,
+                      tab_bar);
+        }
+        bool tabs_ready = false;
+        for (int hh = 0; hh < nblk; ++hh) {
+          const int proj = (b + hh) / p.n_heads;
+#pragma unroll 1
+          for (int g = 0; g < 2; ++g) {
+            const int cg = half * 32 + g * 16;  // head column of a[0]; RoPE partners at cg + 64
+            const int ca = hh * 128 + cg;
+            float a[16], bv[16];
+            __syncwarp();
+            tmem_ld_32x32b_x16(t_base + ca, a);
+            tmem_ld_32x32b_x16(t_base + ca + 64, bv);
+            for (int q = pair_id + 1; q < q_end; ++q) {
+              const float4* part = reinterpret_cast<const float4*>(p.partials) +
+                                   static_cast<size_t>(q * 2 + rank) * (kQ2PartialFloats / 4);
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                const float4 x = __ldcg(part + ((ca + j) >> 2) * kQkvBM + r_tile);
+                const float4 y = __ldcg(part + ((ca + 64 + j) >> 2) * kQkvBM + r_tile);
+                a[j] += x.x;
+                a[j + 1] += x.y;
+                a[j + 2] += x.z;
+                a[j + 3] += x.w;
+                bv[j] += y.x;
+                bv[j + 1] += y.y;
+                bv[j + 2] += y.z;
+                bv[j + 3] += y.w;
+              }
+            }
+            if (hh == nblk - 1 && g == 1) {
+              // every column of this accumulator has been read
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+            }
+            if (proj < 2 && my_slot >= 0) {
+              if (!tabs_ready) {
+                mbar_wait(tab_bar, 0, p.status, kQkvKernelId);
+                tabs_ready = true;
+              }
+              const uint8_t* trow = tabs + r_tile * kTabStride + cg * 4;
+#pragma unroll
+              for (int i = 0; i < 16; i += 4) {
+                const float4 s1 = *reinterpret_cast<const float4*>(trow + i * 4);
+                const float4 s2 = *reinterpret_cast<const float4*>(trow + 256 + i * 4);
+                const float4 c1 = *reinterpret_cast<const float4*>(trow + 512 + i * 4);
+                const float4 c2 = *reinterpret_cast<const float4*>(trow + 768 + i * 4);
+                const float sa[4] = {s1.x, s1.y, s1.z, s1.w}, sb[4] = {s2.x, s2.y, s2.z, s2.w};
+                const float ca4[4] = {c1.x, c1.y, c1.z, c1.w}, cb4[4] = {c2.x, c2.y, c2.z, c2.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const float x1 = a[i + k], x2 = bv[i + k];
+                  a[i + k] = x1 * ca4[k] - x2 * sa[k];
+                  bv[i + k] = x2 * cb4[k] + x1 * sb[k];
+                }
+              }
+            }
+            uint8_t* orow = outs + (hh * kQkvBM + r_tile) * kOutStride + cg * 2;
+#pragma unroll
+            for (int i = 0; i < 16; i += 8) {
+              uint4 va, vb;
+              va.x = pack_bf16x2(a[i], a[i + 1]);
+              va.y = pack_bf16x2(a[i + 2], a[i + 3]);
+              va.z = pack_bf16x2(a[i + 4], a[i + 5]);
+              va.w = pack_bf16x2(a[i + 6], a[i + 7]);
+              vb.x = pack_bf16x2(bv[i], bv[i + 1]);
+              vb.y = pack_bf16x2(bv[i + 2], bv[i + 3]);
+              vb.z = pack_bf16x2(bv[i + 4], bv[i + 5]);
+              vb.w = pack_bf16x2(bv[i + 6], bv[i + 7]);
+              *reinterpret_cast<uint4*>(orow + i * 2) = va;
+              *reinterpret_cast<uint4*>(orow + 128 + i * 2) = vb;
+            }
+          }
+        }
+        if (rope_tile && !tabs_ready) mbar_wait(tab_bar, 0, p.status, kQkvKernelId);  // no copy left in flight
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (half == 0 && my_slot >= 0) {
+          for (int hh = 0; hh < nblk; ++hh) {
+            const int head_g = b + hh;
+            const int proj = head_g / p.n_heads, head = head_g % p.n_heads;
+            __nv_bfloat16* out = proj == 0 ? p.q_out : (proj == 1 ? p.k_out : p.v_out);
+            const int64_t orow_g = (proj > 0 && p.kv_by_slot) ? my_slot : static_cast<int64_t>(row_base + r_tile);
+            bulk_store(out + orow_g * d + head * 128, outs + (hh * kQkvBM + r_tile) * kOutStride, 256);
+          }
+          bulk_commit();
+          bulk_wait_all();
+        }
+      } else {
+        for (int hh = 0; hh < nblk; ++hh) {
+          const int head_g = b + hh;
+          const int proj = head_g / p.n_heads, head = head_g % p.n_heads;
+          __nv_bfloat16* out = proj == 0 ? p.q_out : (proj == 1 ? p.k_out : p.v_out);
+          const bool by_slot = proj > 0 && p.kv_by_slot;
+          for (int sub = 0; sub < 2; ++sub) {
+            // half 0 takes columns ca.., half 1 their RoPE partners ca + 64..
+            const int ca = hh * 128 + sub * 32 + half * 64;
+            float a[32];
+            __syncwarp();
+            tmem_ld_32x32b_x32(t_base + ca, a);
+            for (int q = pair_id + 1; q < q_end; ++q) {
+              const float4* part = reinterpret_cast<const float4*>(p.partials) +
+                                   static_cast<size_t>(q * 2 + rank) * (kQ2PartialFloats / 4);
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 x = __ldcg(part + ((ca + j) >> 2) * kQkvBM + r_tile);
+                a[j] += x.x;
+                a[j + 1] += x.y;
+                a[j + 2] += x.z;
+                a[j + 3] += x.w;
+              }
+            }
+            if (hh == nblk - 1 && sub == 1) {
+              // every column of this accumulator has been read
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+            }
+            // stage row r_tile: a-columns -> 16-byte units 0..7, partners ->
+            // 8..15, unit ^ (row & 7)
+            float* srow = staging + r_tile * 64 + half * 32;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int pu = u ^ (r_tile & 7);
+              *reinterpret_cast<float4*>(srow + pu * 4) =
+                  make_float4(a[4 * u], a[4 * u + 1], a[4 * u + 2], a[4 * u + 3]);
+            }
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            // 16 rows of this warp's quarter, two per step: half-warp h takes
+            // row 2k + h, lane j = lane & 15 takes head columns c, c + 1
+            // (c = sub * 32 + 2j) and their partners c + 64, c + 65
+            q2_rope_rows(staging, p, quarter, half, lane >> 4, lane & 15, sub * 32 + 2 * (lane & 15), proj < 2,
+                         my_slot, out + head * 128, d, by_slot, row_base);
+            asm volatile("bar.sync 1, 256;" ::: "memory");  // staging free again
+          }
+        }
+      }
+      // the partials were read by every epilogue thread (the barrier above):
+      // clear the contributors' flags for the next launch
+      if (ep_tid == 0)
+        for (int q = pair_id + 1; q < q_end; ++q) p.counters[q * 2 + rank] = 0;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the leader's MMAs read both CTAs' shared memory until here
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kQ2TmemCols);
+  }
+}
+
 namespace {
 
 struct QkvPlan {
@@ -357,6 +837,7 @@ struct QkvPlan {
   int n_tiles;
   int n_units;
   int grid;
+  bool pair;  // CTA-pair stream-K kernel (more than 128 rows)
 };
 
 // Units are spread round-robin over one CTA per SM.  Tiles are 128 columns
@@ -387,6 +868,18 @@ QkvPlan plan_qkv(int32_t n_rows, int32_t d_model, int32_t n_heads) {
   pl.splits = (kb_total + pl.kb_per_split - 1) / pl.kb_per_split;  // no empty splits
   pl.n_units = tiles * pl.splits;
   pl.grid = pl.n_units < sms ? pl.n_units : sms;
+  // CTA pairs for 129-256 rows, where they measured faster (256 rows: 45.9
+  // vs 51.1 us; 384 and 512 rows: 69 vs 55-66 us).  FDLLM_QKV_PAIR=1 / 0
+  // forces them on above 128 rows / off.
+  const int pair_env = env_int("FDLLM_QKV_PAIR", -1);
+  pl.pair = n_rows > 128 && d_model % kQkvBK == 0 && (pair_env < 0 ? n_rows <= 256 : pair_env != 0);
+  if (pl.pair) {
+    pl.splits = 1;
+    pl.kb_per_split = d_model / (kQkvBK * pl.ksub);
+    pl.bn = 128;
+    pl.xrows = 128;
+    pl.grid = 2 * (sms / 2);  // capped at the resident pairs at launch
+  }
   return pl;
 }
 
@@ -396,6 +889,8 @@ QkvPlan plan_qkv(int32_t n_rows, int32_t d_model, int32_t n_heads) {
 constexpr size_t kQkvCounterBytes = 4096;  // 1024 tiles (K splits are requested through FDLLM_QKV_SPLITS)
 
 size_t qkv_ws_bytes(const QkvPlan& pl) {
+  // CTA pairs: flags, then one partial accumulator slot per CTA
+  if (pl.pair) return kQkvCounterBytes + static_cast<size_t>(pl.grid) * kQ2PartialFloats * sizeof(float);
   if (pl.splits <= 1) return 256;
   const size_t tiles = static_cast<size_t>(pl.m_tiles) * pl.n_tiles;
   return kQkvCounterBytes + tiles * pl.splits * kQkvBM * pl.bn * sizeof(float);
@@ -428,11 +923,12 @@ int launch_qkv(const void* xn, const void* wq, const void* wk, const void* wv, c
   for (const void* q : ptrs)
     if (q == nullptr || !aligned16(q)) return FDLLM_ERR_ARG;
   const QkvPlan pl = plan_qkv(n_rows, d_model, n_heads);
-  if (pl.splits > 1 && (workspace == nullptr || workspace_bytes < qkv_ws_bytes(pl))) return FDLLM_ERR_WORKSPACE;
+  if ((pl.splits > 1 || pl.pair) && (workspace == nullptr || workspace_bytes < qkv_ws_bytes(pl)))
+    return FDLLM_ERR_WORKSPACE;
   CUtensorMap mx, mq, mk, mv;
   int rc;
   if ((rc = make_tmap_bf16_sw128(&mx, xn, n_rows, d_model, d_model, pl.xrows)) != FDLLM_OK) return rc;
-  const uint32_t wbox = pl.bn == 128 ? 128 : pl.bn / 2;
+  const uint32_t wbox = pl.pair ? 64 : (pl.bn == 128 ? 128 : pl.bn / 2);
   if ((rc = make_tmap_bf16_sw128(&mq, wq, d_model, d_model, d_model, wbox)) != FDLLM_OK) return rc;
   if ((rc = make_tmap_bf16_sw128(&mk, wk, d_model, d_model, d_model, wbox)) != FDLLM_OK) return rc;
   if ((rc = make_tmap_bf16_sw128(&mv, wv, d_model, d_model, d_model, wbox)) != FDLLM_OK) return rc;
@@ -454,10 +950,42 @@ int launch_qkv(const void* xn, const void* wq, const void* wk, const void* wv, c
   p.m_tiles = pl.m_tiles;
   p.n_units = pl.n_units;
   p.ksub = pl.ksub;
-  if (pl.splits > 1) {
+  if (pl.pair) {
+    if (static_cast<size_t>(pl.grid) * sizeof(int32_t) > kQkvCounterBytes) return FDLLM_ERR_ARG;
+    p.counters = static_cast<int32_t*>(workspace);
+    p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kQkvCounterBytes);
+  } else if (pl.splits > 1) {
     if (static_cast<size_t>(pl.m_tiles) * pl.n_tiles * sizeof(int32_t) > kQkvCounterBytes) return FDLLM_ERR_ARG;
     p.counters = static_cast<int32_t*>(workspace);
     p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kQkvCounterBytes);
+  }
+  if (pl.pair) {
+    // One pair per two SMs, capped at the number of pairs that are resident
+    // at once (a GPC with an odd SM count leaves one SM out).
+    static int max_pairs[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64) return FDLLM_ERR_ARG;
+    if (max_pairs[dev] == 0) {
+      if (cudaFuncSetAttribute(qkv2_rope_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQ2Smem) != cudaSuccess)
+        return FDLLM_ERR_CUDA;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(pl.grid), 1, 1);
+      cfg.blockDim = dim3(kQ2Threads, 1, 1);
+      cfg.dynamicSmemBytes = kQ2Smem;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, qkv2_rope_kernel, &cfg) != cudaSuccess || n <= 0) return FDLLM_ERR_CUDA;
+      max_pairs[dev] = n;
+    }
+    // every pair gets a non-empty iteration range; all pairs are resident
+    // at once (owners wait on the partials of later pairs)
+    const long long iters = static_cast<long long>((n_rows + 2 * kQkvBM - 1) / (2 * kQkvBM)) *
+                            ((3 * n_heads + 1) / 2) * (d_model / kQkvBK);
+    int pairs = pl.grid / 2 < max_pairs[dev] ? pl.grid / 2 : max_pairs[dev];
+    if (iters < pairs) pairs = static_cast<int>(iters);
+    if (iters > (1ll << 30)) return FDLLM_ERR_ARG;
+    qkv2_rope_kernel<<<2 * pairs, kQ2Threads, kQ2Smem, stream>>>(mx, mq, mk, mv, p);
+    return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
   }
   if (pl.ksub == 2) {
     if (pl.bn == 128)
@@ -553,7 +1081,7 @@ extern "C" int fdllm_qkv_rope_cache_noalloc(const void* xn, const void* wq, cons
   if (n_rows < 0 || n_heads <= 0 || d_model != n_heads * 128 || n_slots <= 0) return FDLLM_ERR_ARG;
   if (n_rows == 0) return FDLLM_OK;
   const QkvPlan pl = plan_qkv(n_rows, d_model, n_heads);
-  if (pl.splits > 1 && qkv_ws_bytes(pl) > kQkvNoAllocScratchBytes) return FDLLM_ERR_SCRATCH_LIMIT;
+  if ((pl.splits > 1 || pl.pair) && qkv_ws_bytes(pl) > kQkvNoAllocScratchBytes) return FDLLM_ERR_SCRATCH_LIMIT;
   void* scratch = qkv_noalloc_scratch();
   if (scratch == nullptr) return FDLLM_ERR_CUDA;
   if (pl.splits > 1 && cudaMemsetAsync(scratch, 0, kQkvCounterBytes, stream) != cudaSuccess) return FDLLM_ERR_CUDA;

@@ -89,8 +89,9 @@ def sort_desc_stable(x: torch.Tensor) -> torch.Tensor:
 def accept_count(p: torch.Tensor, threshold: float, min_keep: int = 1) -> int:
     """``keep = max(#(p >= threshold), 1)`` (generate.py:231-233, 344-346).
     ``min_keep`` > 1 is the forced-accept harness knob (not a reference
-    feature)."""
-    return max(int((p >= threshold).sum()), min_keep)
+    feature); a forced count never exceeds the window (with ``min_keep`` = 1
+    and a non-empty window the clamp never applies)."""
+    return min(max(int((p >= threshold).sum()), min_keep), p.numel())
 
 
 def verify_keep(p_draft: torch.Tensor, gamma: float) -> int:

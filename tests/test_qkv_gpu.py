@@ -52,6 +52,9 @@ def _oracle(x, w, pos, kc, vc, sin, cos, n_heads):
     (129, 256, 512, {}),
     (300, 512, 1024, {"FDLLM_QKV_BN": "64"}),
     (512, 4096, 1024, {}),
+    (256, 4096, 1024, {}),                                   # CTA-pair stream-K kernel (129-256 rows)
+    (300, 512, 1024, {"FDLLM_QKV_PAIR": "1"}),               # ... forced: a half-empty 256-row block
+    (512, 4096, 1024, {"FDLLM_QKV_PAIR": "1"}),              # ... forced: partial tiles, owner fix-ups
 ])
 def test_qkv_rope_cache_matches_oracle(n_rows, d_model, n_slots, env, monkeypatch):
     import flash_dllm_b200.ops as ops

@@ -44,11 +44,12 @@ def _noalloc(lib, x, w, pos, sin, cos, q, kc, vc, n_heads):
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
 
 
-def test_noalloc_matches_workspace_entry_point_twice(monkeypatch):
+@pytest.mark.parametrize("n_rows", [64, 256])  # split-K / CTA-pair stream-K partials: both use the scratch
+def test_noalloc_matches_workspace_entry_point_twice(n_rows, monkeypatch):
     import flash_dllm_b200.ops as ops
     from flash_dllm_b200._lib import check_device_status, lib
-    monkeypatch.setenv("FDLLM_QKV_SPLITS", "3")  # split-K: the partial sums use the scratch
-    n_rows, d_model, n_slots = 64, 4096, 512   # BASELINE config 1 shape
+    monkeypatch.setenv("FDLLM_QKV_SPLITS", "3")  # split-K at 64 rows (BASELINE config 1 shape)
+    d_model, n_slots = 4096, 512
     n_heads = d_model // 128
     x, w, pos, kc0, vc0, sin, cos = _inputs(n_rows, d_model, n_slots, seed=11)
     q_ref = torch.empty_like(x)
@@ -67,6 +68,7 @@ def test_noalloc_matches_workspace_entry_point_twice(monkeypatch):
 
 def test_noalloc_refuses_requests_beyond_its_scratch(monkeypatch):
     from flash_dllm_b200._lib import lib
+    monkeypatch.setenv("FDLLM_QKV_PAIR", "0")  # the single-CTA kernel,
     monkeypatch.setenv("FDLLM_QKV_SPLITS", "4")  # 256 rows x 4 K-splits: ~50 MB of partials > 24 MiB
     x, w, pos, kc, vc, sin, cos = _inputs(256, 4096, 512, seed=12)
     q = torch.empty_like(x)
