@@ -400,6 +400,19 @@ __device__ __forceinline__ int q2_lo(int pair, int n_pairs, int iters) {
   return static_cast<int>(static_cast<long long>(pair) * iters / n_pairs);
 }
 
+// Segment k of the iteration range [lo, hi) (k < q2_nsegs): the k-blocks of
+// one tile, in range order.
+__device__ __forceinline__ int q2_nsegs(int lo, int hi, int kbt) { return lo < hi ? (hi - 1) / kbt - lo / kbt + 1 : 0; }
+
+__device__ __forceinline__ Q2Seg q2_seg_at(int lo, int hi, int kbt, int k) {
+  Q2Seg s;
+  s.tile = lo / kbt + k;
+  s.k0 = k == 0 ? lo % kbt : 0;
+  const int end = hi - s.tile * kbt;
+  s.k1 = end < kbt ? end : kbt;
+  return s;
+}
+
 // Next segment of the iteration range [i, hi): the k-blocks of one tile.
 __device__ __forceinline__ bool q2_next(int& i, int hi, int kbt, Q2Seg& s) {
   if (i >= hi) return false;
@@ -594,14 +607,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kQ2Threads, 1)
     const int r_tile = quarter * 32 + lane;  // this thread's TMEM lane / tile row
     const int ep_tid = threadIdx.x - 128;
     const int d = p.d_model;
-    int i_unit = 0;
-    int i = lo;
-    Q2Seg sg;
-    while (q2_next(i, hi, kbt, sg)) {
-      const bool last = i >= hi;
+    // Epilogues run in range order, except that an owner part ending the
+    // range is finished before the whole tile in front of it: both then run
+    // after the last MMA, with the ring idle (thread-per-row path).
+    const int n_segs = q2_nsegs(lo, hi, kbt);
+    bool swap_last = false;
+    if (n_segs >= 2) {
+      const Q2Seg s_last = q2_seg_at(lo, hi, kbt, n_segs - 1), s_prev = q2_seg_at(lo, hi, kbt, n_segs - 2);
+      swap_last = s_last.k1 < kbt && s_prev.k0 == 0 && s_prev.k1 == kbt;
+    }
+    uint32_t tab_phase = 0;
+    for (int e = 0; e < n_segs; ++e) {
+      const int m_idx = (swap_last && e >= n_segs - 2) ? 2 * n_segs - 3 - e : e;  // MMA order of the segment
+      const Q2Seg sg = q2_seg_at(lo, hi, kbt, m_idx);
+      const bool last = e == n_segs - 1 || (swap_last && e == n_segs - 2);  // after the last MMA
       const int m_pair = sg.tile % m_pairs, b = (sg.tile / m_pairs) * 2;
       const int nblk = n_blocks - b < 2 ? n_blocks - b : 2;
-      const int acc = i_unit & 1;
+      const int acc = m_idx & 1;
       const uint32_t t_base = tmem_base + acc * kQ2AccCols + (static_cast<uint32_t>(quarter * 32) << 16);
       // row slot, and its RoPE rows pulled into L2 while the MMAs run (the
       // epilogue's table reads are otherwise serialised DRAM round trips)
@@ -620,11 +642,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kQ2Threads, 1)
           }
         }
       }
-      if (!mbar_wait(&acc_full[acc], (i_unit >> 1) & 1, p.status, kQkvKernelId)) *abort_flag = 1;
+      if (!mbar_wait(&acc_full[acc], (m_idx >> 1) & 1, p.status, kQkvKernelId)) *abort_flag = 1;
       asm volatile("bar.sync 1, 256;" ::: "memory");
       if (*abort_flag != 0) break;
       tc_fence_after();
-      ++i_unit;
       if (sg.k0 > 0) {
         // contributor: store the partial sums ([col / 4][row][4] fp32, so a
         // warp's accesses are 512 contiguous bytes) and publish them
@@ -710,7 +731,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kQ2Threads, 1)
             }
             if (proj < 2 && my_slot >= 0) {
               if (!tabs_ready) {
-                mbar_wait(tab_bar, 0, p.status, kQkvKernelId);
+                mbar_wait(tab_bar, tab_phase & 1, p.status, kQkvKernelId);
                 tabs_ready = true;
               }
               const uint8_t* trow = tabs + r_tile * kTabStride + cg * 4;
@@ -747,7 +768,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kQ2Threads, 1)
             }
           }
         }
-        if (rope_tile && !tabs_ready) mbar_wait(tab_bar, 0, p.status, kQkvKernelId);  // no copy left in flight
+        if (rope_tile && !tabs_ready) mbar_wait(tab_bar, tab_phase & 1, p.status, kQkvKernelId);  // no copy in flight
+        if (rope_tile) ++tab_phase;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("bar.sync 1, 256;" ::: "memory");
         if (half == 0 && my_slot >= 0) {
@@ -761,6 +783,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kQ2Threads, 1)
           bulk_commit();
           bulk_wait_all();
         }
+        asm volatile("bar.sync 1, 256;" ::: "memory");  // the staged rows were read: tables / rows reusable
       } else {
         for (int hh = 0; hh < nblk; ++hh) {
           const int head_g = b + hh;
