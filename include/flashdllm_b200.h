@@ -93,10 +93,11 @@ int fdllm_qkv_rope_cache(const void* xn, const void* wq, const void* wk, const v
  * once loaded): same arguments and results minus the workspace, whose role is taken by a fixed
  * 24 MiB array inside the library (held on every GPU that loads it until exit).  No counterpart
  * in the reference.  Calls needing more split-K scratch than that (d_model 4096: more than 128
- * rows with a K split) return FDLLM_ERR_SCRATCH_LIMIT without launching.  The first call on a
+ * rows with a requested K split) return FDLLM_ERR_SCRATCH_LIMIT without launching; the partial
+ * sums of the CTA-pair kernel (129-256 rows, one 128 KB slot per CTA) fit.  The first call on a
  * device looks up the array's address; make it before any stream capture.  Calls share the
- * array (its counters are cleared on entry), so calls that overlap on the GPU race: serialise
- * them.  Allocates nothing. */
+ * array (split-K counters are cleared on entry; the CTA-pair kernel leaves its flags at zero),
+ * so calls that overlap on the GPU race: serialise them.  Allocates nothing. */
 int fdllm_qkv_rope_cache_noalloc(const void* xn, const void* wq, const void* wk, const void* wv, const int64_t* pos,
                                  const float* rope_sin, const float* rope_cos, void* q_out, void* k_cache,
                                  void* v_cache, int32_t n_rows, int32_t d_model, int32_t n_heads, int64_t n_slots,
@@ -138,7 +139,9 @@ size_t fdllm_attn_workspace_bytes(int32_t max_items, int32_t n_heads, int32_t kv
  *   attn_scores  fp32 [batch*seqlen_max] or NULL: when given, for every key n of sequence b
  *              attn_scores[b*seqlen_max + n] += score_scale * sum over masked rows and heads of the
  *              raw (unscaled) q.k logit -- the reference's S tensor + S.mean((0,1)) fused.
- *   kv_splits  split of each sequence's key range over CTAs (1 = none; partials combined on device)
+ *   kv_splits  split of each item's key range over CTAs: 1 = none; the tcgen05 kernel runs 2, 4 or 8
+ *              (other counts round down) as one cluster of CTAs per item pair, merged in distributed
+ *              shared memory; the workspace holds partials only for the mma.sync comparison kernel
  * ref llada/flash_cache_triton.py:103-252 (_flash_masked_attention_fwd, _flash_tracked_attention_fwd)
  * and :538, :614-615 (S and attn_scores). */
 int fdllm_attn_cache(const void* q, void* o, const void* k_cache, const void* v_cache, const void* plan,
