@@ -636,6 +636,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int head = blockIdx.y;
+  // Q, the K/V rows and the plan come from the kernels before (programmatic
+  // launch: this CTA may already be resident while the QKV GEMM finishes)
+  pdl_wait();
 
   // warp -> (half, role): 0,1 softmax h0 | 2,3 softmax h1 | 4 scores h1 |
   // 5 MMA h0 | 6 scores h0 | 7 MMA h1 | 8 K h0 | 9 V h0 | 10 K h1 | 11 V h1
@@ -1322,24 +1325,9 @@ int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap&
     // one CTA = two work items; key splits as clusters of CTAs
     p.kv_splits = tc_splits(p.kv_splits);
     const dim3 grid(static_cast<unsigned>((grid_items + 1) / 2 * p.kv_splits), static_cast<unsigned>(p.n_heads), 1);
-    if (p.kv_splits == 1) {
-      attn_tc_kernel<kVerify><<<grid, kTcThreads, kTcSmem, stream>>>(mk, mv, mk1, mv1, p);
-    } else {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = grid;
-      cfg.blockDim = dim3(kTcThreads, 1, 1);
-      cfg.dynamicSmemBytes = kTcSmem;
-      cfg.stream = stream;
-      cudaLaunchAttribute attr_c[1];
-      attr_c[0].id = cudaLaunchAttributeClusterDimension;
-      attr_c[0].val.clusterDim.x = static_cast<unsigned>(p.kv_splits);
-      attr_c[0].val.clusterDim.y = 1;
-      attr_c[0].val.clusterDim.z = 1;
-      cfg.attrs = attr_c;
-      cfg.numAttrs = 1;
-      if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<kVerify>, mk, mv, mk1, mv1, p) != cudaSuccess)
-        return FDLLM_ERR_CUDA;
-    }
+    if (launch_ex(attn_tc_kernel<kVerify>, grid, dim3(kTcThreads), kTcSmem, stream,
+                  static_cast<unsigned>(p.kv_splits), pdl_enabled(), mk, mv, mk1, mv1, p) != cudaSuccess)
+      return FDLLM_ERR_CUDA;
     return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
   }
   if (p.kv_splits > 1) {

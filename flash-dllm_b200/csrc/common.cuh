@@ -382,6 +382,15 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {
                : "memory");
 }
 
+// ---------------------------------------------- programmatic dependent launch ----
+// A kernel launched with cudaLaunchAttributeProgrammaticStreamSerialization
+// may start while the kernel before it in the stream still runs; pdl_wait()
+// blocks until that kernel has completed and its memory is visible (a no-op
+// for a normal launch).  pdl_launch_dependents() lets the next kernel start
+// early (it still waits for this one's completion before reading).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 // ------------------------------------------------------------------ misc ----
 // The PTX ex2.approx.ftz.f32 instruction (2^x; -inf -> +0, tiny results flush
 // to zero), as flash-attention softmax kernels use it.

@@ -44,6 +44,7 @@ __global__ void __launch_bounds__(kNormThreads) norm_rows_kernel(const __nv_bflo
                                                                  __nv_bfloat16* __restrict__ y,
                                                                  __nv_bfloat16* __restrict__ h, int dim, float eps) {
   __shared__ float red[kNormThreads / 32];
+  pdl_launch_dependents();  // the QKV GEMM may set up while the rows are normalised
   const int64_t base = static_cast<int64_t>(blockIdx.x) * dim;
   const uint4* xr = reinterpret_cast<const uint4*>(x + base);
   const uint4* rr = reinterpret_cast<const uint4*>(r + base);

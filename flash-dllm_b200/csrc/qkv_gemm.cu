@@ -126,6 +126,9 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the normalised rows come from the kernel before (programmatic launch)
+  pdl_wait();
+  pdl_launch_dependents();
   const int units_per_head = p.n_heads * kPerHead;
 
   if (warp == 0) {
@@ -520,6 +523,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kQ2Threads, 1)
   cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the normalised rows come from the kernel before (programmatic launch)
+  pdl_wait();
+  pdl_launch_dependents();
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kQ2RegsLow));
   if (warp == 0) {
@@ -932,7 +938,9 @@ int launch_qkv_cfg(const CUtensorMap& mx, const CUtensorMap& mq, const CUtensorM
       return FDLLM_ERR_CUDA;
     attr_set[dev] = true;
   }
-  qkv_rope_kernel<BN, XROWS, KSUB><<<pl.grid, kQkvThreads, C::kSmem, stream>>>(mx, mq, mk, mv, p);
+  if (launch_ex(qkv_rope_kernel<BN, XROWS, KSUB>, dim3(pl.grid), dim3(kQkvThreads), C::kSmem, stream, 1,
+                pdl_enabled(), mx, mq, mk, mv, p) != cudaSuccess)
+    return FDLLM_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
 }
 
@@ -1007,7 +1015,9 @@ int launch_qkv(const void* xn, const void* wq, const void* wk, const void* wv, c
     int pairs = pl.grid / 2 < max_pairs[dev] ? pl.grid / 2 : max_pairs[dev];
     if (iters < pairs) pairs = static_cast<int>(iters);
     if (iters > (1ll << 30)) return FDLLM_ERR_ARG;
-    qkv2_rope_kernel<<<2 * pairs, kQ2Threads, kQ2Smem, stream>>>(mx, mq, mk, mv, p);
+    if (launch_ex(qkv2_rope_kernel, dim3(2 * pairs), dim3(kQ2Threads), kQ2Smem, stream, 1, pdl_enabled(), mx, mq,
+                  mk, mv, p) != cudaSuccess)
+      return FDLLM_ERR_CUDA;
     return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
   }
   if (pl.ksub == 2) {
