@@ -963,6 +963,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int64_t base = static_cast<int64_t>(it.seq) * p.block_rows + it.chunk_row0;
       mrow = p.mask + (base + min(r, max(it.rows - 1, 0))) * p.block_rows;
     }
+    // verify: the row's first 64 in-block mask bytes, loaded while the cache
+    // tiles run (the in-block tiles come last)
+    uint4 mask_w[4] = {};
+    const bool mask_pre = kVerify && has_item && it.blk_rows > 0 && p.block_rows % 16 == 0 &&
+                          (reinterpret_cast<uintptr_t>(mrow) & 15) == 0;
+    if (mask_pre) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k)  // within this row's block_rows bytes
+        if (16 * k < it.blk_rows && 16 * k + 16 <= p.block_rows)
+          mask_w[k] = __ldg(reinterpret_cast<const uint4*>(mrow) + k);
+    }
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
@@ -981,8 +992,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int n0 = blk ? (t - nt_cache) * kKeyTile : c0 + t * kKeyTile;
       const int n_valid = (blk ? it.blk_rows : c1) - n0;
       const bool full = n_valid >= kKeyTile;  // uniform
-      if (blk) {
+      if (blk && n0 == 0 && mask_pre) {
         // the block's own keys: key range and the verify mask of this row
+        const uint8_t* mb = reinterpret_cast<const uint8_t*>(mask_w);
+#pragma unroll
+        for (int j = 0; j < 64; ++j) sv[j] = (j < n_valid && mb[j] != 0) ? sv[j] : -INFINITY;
+      } else if (blk) {
 #pragma unroll
         for (int j = 0; j < 64; ++j) sv[j] = (j < n_valid && __ldg(mrow + n0 + j) != 0) ? sv[j] : -INFINITY;
       } else if (!full) {
