@@ -147,8 +147,6 @@ __device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src,
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// the source shared memory of every committed bulk store may be rewritten
-__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
@@ -341,11 +339,6 @@ __device__ __forceinline__ float2 ld_dsmem_f2(uint32_t cluster_addr) {
 // memory (same offsets); each CTA's TMEM receives its half of D.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_addr, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr),
-               "r"(bytes)
-               : "memory");
 }
 // 2-D tiled load into this CTA's shared memory whose completion bytes are
 // counted on an mbarrier given by cluster address (the pair leader's)
