@@ -18,7 +18,15 @@
 // Split units of one tile run on different CTAs at the same time; each writes
 // its fp32 partial to the caller's workspace and the last to arrive (atomic
 // counter) adds the others in split order, runs the epilogue and resets the
-// counter for the next call.
+// counter for the next call.  (K splits only on request: whole-K tiles
+// measured faster at every row count.)
+//
+// qkv2_rope_kernel (further down): the CTA-pair variant used for 129-256
+// rows -- 2-SM UMMAs on 256 x 256 tiles, stream-K over (tile, k-block).
+//
+// Both kernels are launched programmatically dependent on the kernel before
+// them (the RMSNorm producing X) and let the attention kernel after them
+// launch early; they wait for X before their first load.
 #include "common.cuh"
 #include "internal.h"
 
