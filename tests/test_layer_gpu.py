@@ -130,3 +130,17 @@ def test_add_rmsnorm_and_swiglu():
     out = ops.swiglu(gu[:, :256], gu[:, 256:])
     ref = torch.nn.functional.silu(gu[:, :256].float()).bfloat16() * gu[:, 256:]
     assert _rel(out, ref) <= 1e-2
+
+
+def test_plain_launches_without_programmatic_dependency():
+    """FDLLM_PDL=0 launches the QKV and attention kernels without programmatic
+    stream serialisation (read once per process, hence a child process)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, FDLLM_PDL="0")
+    r = subprocess.run([sys.executable, "-c", "import __graft_entry__ as g; g.smoke()"], cwd=root, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "smoke ok" in r.stdout
