@@ -14,7 +14,8 @@
  * "bf16" means __nv_bfloat16 / torch.bfloat16.  The library allocates no
  * device memory: callers pass workspaces sized by the *_workspace_bytes()
  * queries (zero-filled once before first use; the kernels leave them ready
- * for the next call).
+ * for the next call, except after a call whose device status reported an
+ * error: zero the workspace again before reusing it).
  *
  * Citations "ref file:line" name the reference interface each entry point
  * replaces (VILA-Lab/Flash-dLLM).
