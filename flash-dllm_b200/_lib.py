@@ -30,6 +30,7 @@ SIGNATURES = {
     "fdllm_rmsnorm": (_int, [_p, _p, _p, _i32, _i32, _f32, _p]),
     "fdllm_add_rmsnorm": (_int, [_p, _p, _p, _p, _p, _i32, _i32, _f32, _p]),
     "fdllm_swiglu": (_int, [_p, _p, _p, _i64, _i32, _i64, _p]),
+    "fdllm_qkv_set_plan": (_int, [_i32, _i32, _i32, _i32]),
     "fdllm_qkv_workspace_bytes": (_sz, [_i32, _i32, _i32]),
     "fdllm_qkv_rope_cache": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i64, _p, _sz, _p]),
     "fdllm_qkv_rope_cache_noalloc": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i64, _p]),
@@ -38,8 +39,8 @@ SIGNATURES = {
     "fdllm_attn_plan_bytes": (_sz, [_i32, _i32]),
     "fdllm_plan_cache_attention": (_int, [_p, _i32, _p, _i32, _i32, _i32, _i32, _i32, _p, _sz, _p]),
     "fdllm_attn_workspace_bytes": (_sz, [_i32, _i32, _i32]),
-    "fdllm_attn_cache": (_int, [_p, _p, _p, _p, _p, _i32, _p, _f32, _i32, _i32, _i32, _i64, _f32, _i32, _p, _sz,
-                                _p]),
+    "fdllm_attn_cache": (_int, [_p, _p, _p, _p, _p, _i32, _p, _f32, _i32, _i32, _i32, _i64, _f32, _i32, _p, _i32,
+                                _p, _sz, _p]),
     "fdllm_verify_attn": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32, _i64,
                                  _f32, _i32, _p, _sz, _p]),
     "fdllm_row_stats": (_int, [_p, _i64, _i32, _i32, _p, _p, _p, _p, _p]),
@@ -93,10 +94,27 @@ def stream_handle(device=None) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_ERROR_HOOKS = []
+
+
+def on_device_error(fn) -> None:
+    """Register ``fn()`` to run when :func:`check_device_status` finds an
+    error (before it raises): the workspace owner re-zeroes its buffers."""
+    _ERROR_HOOKS.append(fn)
+
+
 def check_device_status(stream=None) -> None:
-    """Synchronise and raise if any kernel recorded a device-side error."""
+    """Synchronise and raise if any kernel recorded a device-side error.
+
+    A kernel that stopped on an error can leave split-K counters or CTA-pair
+    handoff flags set in its workspace; the registered hooks zero the
+    workspaces in place (same addresses, so captured CUDA graphs stay valid)
+    before the error is raised, so a caller that catches it can go on."""
     out = (C.c_int32 * 4)()
     s = stream if stream is not None else stream_handle()
     call("fdllm_status_read", C.cast(out, C.c_void_p), s)
     if out[0] != 0:
+        for fn in _ERROR_HOOKS:
+            fn()
+        torch.cuda.synchronize()
         raise FdllmError(f"device kernel {out[2]}", out[0], out[1])

@@ -1,22 +1,26 @@
 // Block-table scheduled attention over the KV cache (Flash-Cache) and the
-// Flash-Verify attention, as one warp-specialised kernel template.
+// Flash-Verify attention, as one warp-specialised tcgen05 kernel template
+// (attn_tc_kernel), plus the planner that turns the reference's block tables
+// into work items and the fixed-order reduction of the attention-importance
+// scores.
 //
 // Work item = up to 64 query rows of one sequence x one head x one slice of
 // that sequence's keys.  For Flash-Cache an item holds the sequence's masked
 // rows first and then its tracked (refresh) rows, so masked and tracked rows
-// share one pass over K/V (the reference runs two kernels, two passes).
+// share one pass over K/V (the reference runs two kernels, two passes).  The
+// kernel's structure is described above attn_tc_kernel.
 //
-// CTA = 5 warps.  Warp 4 is the producer: it stages 64-key K and V tiles
-// (128-byte-swizzled rows, 2 x 8 KB halves per tile) into a 3-deep smem ring --
-// with TMA box loads for contiguous cache ranges, or with 16-byte cp.async
-// gathers (zero-filling invalid keys) for the verify key list and the verify
-// block's own K/V.  Warps 0-3 each own 16 query rows: Q fragments stay in
-// registers, S = Q K^T and O += P V run on mma.sync m16n8k16 (bf16 in, fp32
-// accumulate) with ldmatrix from the swizzled tiles, P never leaves
-// registers, and the online softmax works in the exp2 domain.  When masked
-// rows are present the raw (unscaled) logits of those rows are summed per
-// key across the warp and added to attn_scores (the reference's S tensor and
-// S.mean((0,1)) fused into one atomic per key, warp and head).
+// Keys of a sequence live either in its contiguous cache region
+// [seq * seqlen_max, seq * seqlen_max + k_end) (the reference's layout) or,
+// with a page table, in 64-row pages: key n of sequence b is cache row
+// pages[b * pages_per_seq + n / 64] * 64 + n % 64.  A 64-key tile is one page,
+// so either way a tile is one pair of TMA boxes.
+//
+// attn_scores: every (item, head) CTA writes the raw-logit column sums of its
+// masked rows into its own slice of a workspace (no atomics); a second small
+// kernel adds them to attn_scores in a fixed order (chunks, then heads), so
+// the scores -- and every refresh decision taken from them -- are the same
+// on every run.
 #include <cstring>
 
 #include "common.cuh"
@@ -27,18 +31,24 @@ namespace fdllm {
 constexpr int kHD = 128;
 constexpr int kItemRows = 64;
 constexpr int kKeyTile = 64;
-constexpr int kAttnStages = 3;
-constexpr int kComputeWarps = 4;
-constexpr int kAttnThreads = (kComputeWarps + 1) * 32;
 constexpr int kHalfBytes = kKeyTile * 128;          // 64 rows x 128 B (64 dims)
 constexpr int kTileBytes = 2 * kHalfBytes;          // one K or V tile (128 dims)
-constexpr int kAttnStageBytes = 2 * kTileBytes;     // K + V
-constexpr int kAttnBarOffset = kAttnStages * kAttnStageBytes;
-constexpr int kAttnSmem = 1024 + kAttnBarOffset + 128;
+// Plan layout (int32): header, then `capacity` items of kPlanItem, then
+// kPlanSeq ints per sequence.
+//   header:   [0] items, [1] batch, [2] items holding masked rows ("masked
+//             items", numbered in item order), [3] offset of the per-sequence
+//             section
+//   item:     [0] seq, [1] k_end, [2] masked row start, [3] masked rows,
+//             [4] tracked row start, [5] tracked rows, [6] masked-item number
+//             (-1: no masked rows), [7] 0
+//   sequence: [0] number of its first masked item, [1] its masked items
+//             (consecutive), [2] k_end (0: no rows)
 constexpr int kPlanHeader = 8;
 constexpr int kPlanItem = 8;
+constexpr int kPlanSeq = 3;
 constexpr int kAttnKernelId = 2;
 constexpr int kPlanKernelId = 3;
+constexpr int kScoresKernelId = 6;
 
 // Byte offset of 16-byte chunk `chunk` (0..15, 8 dims each) of key row `row`
 // inside a tile stored as two 64-dim halves with the 128-byte swizzle -- the
@@ -47,23 +57,6 @@ __device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
   return (chunk >> 3) * kHalfBytes + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
 }
 
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 // 16-byte async copy; with valid == false nothing is read and 16 zero bytes land.
 __device__ __forceinline__ void cp_async_16_zfill(void* smem_dst, const void* gmem_src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
@@ -82,9 +75,8 @@ struct AttnParams {
   const int32_t* vblocks;       // verify mode: (k_s, k_e, q_s, q_e) rows
   const int64_t* pos_k;         // verify mode: gathered key slots
   const uint8_t* mask;          // verify mode: [n_blocks*block_rows, block_rows]
-  float* scores;                // cache mode, optional
-  float* part_o;                // split-KV partials [item][head][split][64][128]
-  float* part_ml;               // [item][head][split][64][2]
+  float* colsum;                // cache mode with scores: [masked item][head][seqlen_max] fp32 column sums
+  const int32_t* pages;         // cache mode, optional: page table [batch][pages_per_seq]
   int32_t* status;
   int64_t n_slots;
   int64_t n_pos_k;
@@ -98,6 +90,7 @@ struct AttnParams {
   int32_t block_rows;           // verify mode
   int32_t row_chunks;           // verify mode: ceil(block_rows / 64)
   int32_t n_rows;               // rows of q / o (and of k1 / v1 in verify mode)
+  int32_t pages_per_seq;        // cache mode with a page table
 };
 
 // Item description resolved by every thread of the CTA.
@@ -110,6 +103,7 @@ struct Item {
   int blk_rows;     // verify: rows of the block, also its in-block key count
   int blk_q0;       // verify: first row of the block (q_s)
   int chunk_row0;   // verify: first block row of this item (64 * chunk)
+  int mchunk;       // cache: masked-item number of the item (-1: no masked rows)
 };
 
 __device__ __forceinline__ int item_row(const Item& it, int r) {
@@ -126,6 +120,7 @@ __device__ __forceinline__ bool load_item(const AttnParams& p, bool verify, int 
     it.m_len = e[3];
     it.t_start = e[4];
     it.rows = e[3] + e[5];
+    it.mchunk = e[6];
     return it.rows > 0;
   }
   if (item_id >= p.n_items) return false;
@@ -151,324 +146,9 @@ __device__ __forceinline__ bool load_item(const AttnParams& p, bool verify, int 
   return it.rows > 0;
 }
 
-template <bool kVerify>
-__global__ void __launch_bounds__(kAttnThreads, 2)
-    attn_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
-                const AttnParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kAttnBarOffset);
-  uint64_t* empty = full + kAttnStages;
-  int32_t* sflag = reinterpret_cast<int32_t*>(empty + kAttnStages);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int item_id = blockIdx.x;
-  const int head = blockIdx.y;
-  const int split = blockIdx.z;
-
-  Item it{};
-  if (!load_item(p, kVerify, item_id, it)) return;  // uniform across the CTA
-  // keys of this split: equal 64-aligned slices of the item's key range
-  const int per = ((it.n_keys + p.kv_splits - 1) / p.kv_splits + kKeyTile - 1) / kKeyTile * kKeyTile;
-  const int c0 = min(it.n_keys, split * per);
-  const int c1 = min(it.n_keys, c0 + per);
-  const int nt_cache = (c1 - c0 + kKeyTile - 1) / kKeyTile;
-  const bool last_split = split == p.kv_splits - 1;
-  const int nt_blk = (kVerify && last_split) ? (it.blk_rows + kKeyTile - 1) / kKeyTile : 0;
-  const int n_tiles = nt_cache + nt_blk;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kAttnStages; ++s) {
-      mbar_init(&full[s], kVerify ? 32 : 1);
-      mbar_init(&empty[s], kComputeWarps);
-    }
-    sflag[0] = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
-
-  const int64_t d = p.d_model;
-  if (warp == kComputeWarps) {
-    // -------------------------------------------------------- producer ----
-    for (int t = 0; t < n_tiles; ++t) {
-      const int s = t % kAttnStages;
-      const uint32_t ph = (t / kAttnStages) & 1;
-      if (t >= kAttnStages && !mbar_wait(&empty[s], ph ^ 1, p.status, kAttnKernelId)) break;
-      uint8_t* kt = smem + s * kAttnStageBytes;
-      uint8_t* vt = kt + kTileBytes;
-      if (!kVerify) {
-        if (lane == 0) {
-          const int y = it.seq * p.seqlen_max + c0 + t * kKeyTile;
-          mbar_arrive_expect_tx(&full[s], kAttnStageBytes);
-          tma_load_2d(kt, &map_k, head * kHD, y, &full[s]);
-          tma_load_2d(kt + kHalfBytes, &map_k, head * kHD + 64, y, &full[s]);
-          tma_load_2d(vt, &map_v, head * kHD, y, &full[s]);
-          tma_load_2d(vt + kHalfBytes, &map_v, head * kHD + 64, y, &full[s]);
-        }
-      } else {
-        const bool blk = t >= nt_cache;
-        const int n0 = blk ? (t - nt_cache) * kKeyTile : c0 + t * kKeyTile;
-        const int n_end = blk ? it.blk_rows : c1;
-        // Resolve the 64 source rows of this tile first (two per lane, one
-        // coalesced load each), so the gathers below issue back to back.
-        int64_t src_row[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int n = n0 + lane + 32 * h;
-          int64_t row = -1;
-          if (n < n_end) {
-            if (blk) {
-              row = it.blk_q0 + n;
-            } else {
-              const int64_t pk = static_cast<int64_t>(it.k_base) + n;
-              row = (pk < p.n_pos_k) ? p.pos_k[pk] : -1;
-              if (row < 0 || row >= p.n_slots) {
-                report(p.status, FDLLM_ERR_INDEX, static_cast<int>(pk), kAttnKernelId);
-                row = -1;
-              }
-            }
-          }
-          src_row[h] = row;
-        }
-        const __nv_bfloat16* kbase_g = blk ? p.k1 : p.kc;
-        const __nv_bfloat16* vbase_g = blk ? p.v1 : p.vc;
-        // lane covers 16-byte chunk (lane % 16) of keys 2i + lane / 16
-#pragma unroll 8
-        for (int i = 0; i < kKeyTile / 2; ++i) {
-          const int key = 2 * i + (lane >> 4);
-          const int chunk = lane & 15;
-          const int64_t r0 = __shfl_sync(0xffffffffu, src_row[0], key & 31);
-          const int64_t r1 = __shfl_sync(0xffffffffu, src_row[1], key & 31);
-          const int64_t row = key < 32 ? r0 : r1;
-          const bool valid = row >= 0;
-          const int64_t off = valid ? row * d + head * kHD + chunk * 8 : 0;
-          cp_async_16_zfill(kt + tile_off(key, chunk), kbase_g + off, valid);
-          cp_async_16_zfill(vt + tile_off(key, chunk), vbase_g + off, valid);
-        }
-        cp_async_mbar_arrive(&full[s]);
-      }
-    }
-    return;
-  }
-
-  // ------------------------------------------------------------ compute ----
-  const int g = lane >> 2;
-  const int tq = lane & 3;
-  const int r0 = warp * 16 + g;      // item rows of this thread: r0, r0 + 8
-  const int r1 = r0 + 8;
-  const bool v0 = r0 < it.rows, v1 = r1 < it.rows;
-  const int64_t grow0 = v0 ? item_row(it, r0) : 0;
-  const int64_t grow1 = v1 ? item_row(it, r1) : 0;
-  const bool score_rows = (!kVerify) && p.scores != nullptr && (warp * 16 < it.m_len);
-  const float mrow0 = (!kVerify && r0 < it.m_len) ? 1.f : 0.f;
-  const float mrow1 = (!kVerify && r1 < it.m_len) ? 1.f : 0.f;
-
-  // Q fragments (A operand, 16 rows x 128 dims) straight from global memory.
-  uint32_t qa[8][4];
-  {
-    const uint32_t* q0p = reinterpret_cast<const uint32_t*>(p.q + grow0 * d + head * kHD);
-    const uint32_t* q1p = reinterpret_cast<const uint32_t*>(p.q + grow1 * d + head * kHD);
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      qa[kk][0] = v0 ? __ldg(q0p + kk * 8 + tq) : 0u;
-      qa[kk][1] = v1 ? __ldg(q1p + kk * 8 + tq) : 0u;
-      qa[kk][2] = v0 ? __ldg(q0p + kk * 8 + 4 + tq) : 0u;
-      qa[kk][3] = v1 ? __ldg(q1p + kk * 8 + 4 + tq) : 0u;
-    }
-  }
-
-  float oacc[16][4];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  const uint8_t* mrow_ptr0 = nullptr;
-  const uint8_t* mrow_ptr1 = nullptr;
-  if (kVerify) {
-    const int64_t base = static_cast<int64_t>(it.seq) * p.block_rows + it.chunk_row0;
-    mrow_ptr0 = p.mask + (base + min(r0, it.rows - 1)) * p.block_rows;
-    mrow_ptr1 = p.mask + (base + min(r1, it.rows - 1)) * p.block_rows;
-  }
-
-  for (int t = 0; t < n_tiles; ++t) {
-    const int s = t % kAttnStages;
-    const uint32_t ph = (t / kAttnStages) & 1;
-    const bool got = mbar_wait(&full[s], ph, p.status, kAttnKernelId);
-    const bool blk = kVerify && t >= nt_cache;
-    const int n0 = blk ? (t - nt_cache) * kKeyTile : c0 + t * kKeyTile;
-    const int n_valid = (blk ? it.blk_rows : c1) - n0;   // keys of this tile that exist
-    uint8_t* kt = smem + s * kAttnStageBytes;
-    uint8_t* vt = kt + kTileBytes;
-    if (!kVerify && n_valid < kKeyTile) {
-      // TMA brought whole rows past the end of this key range: zero their V so
-      // 0-probability keys cannot inject non-finite cache contents.  Every
-      // compute warp reaches both barriers, including one whose wait ran out.
-      if (!got) sflag[0] = 1;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (sflag[0] == 0) {
-        for (int idx = threadIdx.x; idx < (kKeyTile - n_valid) * 16; idx += 128) {
-          const int key = n_valid + idx / 16, chunk = idx % 16;
-          *reinterpret_cast<uint4*>(vt + tile_off(key, chunk)) = make_uint4(0, 0, 0, 0);
-        }
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (sflag[0] != 0) return;
-    }
-    if (!got) return;
-    const uint32_t kbase = smem_u32(kt), vbase = smem_u32(vt);
-
-    // S = Q K^T  (16 rows x 64 keys per warp)
-    float sacc[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-#pragma unroll
-      for (int jp = 0; jp < 4; ++jp) {
-        const int mi = lane >> 3;
-        const int key = jp * 16 + (mi >> 1) * 8 + (lane & 7);
-        const int chunk = 2 * kk + (mi & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kbase + tile_off(key, chunk), b0, b1, b2, b3);
-        mma_bf16(sacc[2 * jp], qa[kk], b0, b1);
-        mma_bf16(sacc[2 * jp + 1], qa[kk], b2, b3);
-      }
-    }
-
-    // key validity (+ verify in-block mask), raw-score accumulation
-    float colsum[8][2];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int kl = j * 8 + 2 * tq + e;
-        const bool kv_ok = kl < n_valid;
-        bool ok0 = kv_ok, ok1 = kv_ok;
-        if (blk) {
-          const int kj = n0 + kl;
-          ok0 = ok0 && mrow_ptr0[kj] != 0;
-          ok1 = ok1 && mrow_ptr1[kj] != 0;
-        }
-        colsum[j][e] = kv_ok ? (sacc[j][e] * mrow0 + sacc[j][2 + e] * mrow1) : 0.f;
-        sacc[j][e] = ok0 ? sacc[j][e] * p.scale_log2 : -INFINITY;
-        sacc[j][2 + e] = ok1 ? sacc[j][2 + e] * p.scale_log2 : -INFINITY;
-      }
-    }
-    if (score_rows) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float v = colsum[j][e];
-          v += __shfl_xor_sync(0xffffffffu, v, 4);
-          v += __shfl_xor_sync(0xffffffffu, v, 8);
-          v += __shfl_xor_sync(0xffffffffu, v, 16);
-          colsum[j][e] = v;
-        }
-      }
-      if (g == 0) {
-        float* srow = p.scores + static_cast<int64_t>(it.seq) * p.seqlen_max + n0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int kl = j * 8 + 2 * tq + e;
-            if (kl < n_valid) atomicAdd(srow + kl, colsum[j][e] * p.score_scale);
-          }
-      }
-    }
-
-    // online softmax (exp2 domain)
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      mx0 = fmaxf(mx0, fmaxf(sacc[j][0], sacc[j][1]));
-      mx1 = fmaxf(mx1, fmaxf(sacc[j][2], sacc[j][3]));
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float ref0 = mn0 == -INFINITY ? 0.f : mn0;
-    const float ref1 = mn1 == -INFINITY ? 0.f : mn1;
-    const float al0 = exp2f(m0 - ref0), al1 = exp2f(m1 - ref1);
-    m0 = mn0;
-    m1 = mn1;
-    float ps0 = 0.f, ps1 = 0.f;
-    uint32_t pa[4][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float p00 = exp2f(sacc[j][0] - ref0), p01 = exp2f(sacc[j][1] - ref0);
-      const float p10 = exp2f(sacc[j][2] - ref1), p11 = exp2f(sacc[j][3] - ref1);
-      ps0 += p00 + p01;
-      ps1 += p10 + p11;
-      pa[j >> 1][(j & 1) * 2 + 0] = pack_bf16x2(p00, p01);
-      pa[j >> 1][(j & 1) * 2 + 1] = pack_bf16x2(p10, p11);
-    }
-    l0 = l0 * al0 + ps0;
-    l1 = l1 * al1 + ps1;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      oacc[j][0] *= al0;
-      oacc[j][1] *= al0;
-      oacc[j][2] *= al1;
-      oacc[j][3] *= al1;
-    }
-    // O += P V
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int jp = 0; jp < 8; ++jp) {
-        const int mi = lane >> 3;
-        const int key = kk * 16 + (mi & 1) * 8 + (lane & 7);
-        const int chunk = 2 * jp + (mi >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(vbase + tile_off(key, chunk), b0, b1, b2, b3);
-        mma_bf16(oacc[2 * jp], pa[kk], b0, b1);
-        mma_bf16(oacc[2 * jp + 1], pa[kk], b2, b3);
-      }
-    }
-    if (!kVerify) fence_proxy_async_smem();  // generic zero-fill before the next TMA write
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-  }
-
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-
-  if (p.kv_splits == 1) {
-    const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
-    const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
-    __nv_bfloat16* o0 = p.o + grow0 * d + head * kHD;
-    __nv_bfloat16* o1 = p.o + grow1 * d + head * kHD;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if (v0) *reinterpret_cast<uint32_t*>(o0 + j * 8 + 2 * tq) = pack_bf16x2(oacc[j][0] * inv0, oacc[j][1] * inv0);
-      if (v1) *reinterpret_cast<uint32_t*>(o1 + j * 8 + 2 * tq) = pack_bf16x2(oacc[j][2] * inv1, oacc[j][3] * inv1);
-    }
-  } else {
-    const int64_t slot = (static_cast<int64_t>(item_id) * p.n_heads + head) * p.kv_splits + split;
-    float* po = p.part_o + slot * kItemRows * kHD;
-    float* pml = p.part_ml + slot * kItemRows * 2;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      *reinterpret_cast<float2*>(po + r0 * kHD + j * 8 + 2 * tq) = make_float2(oacc[j][0], oacc[j][1]);
-      *reinterpret_cast<float2*>(po + r1 * kHD + j * 8 + 2 * tq) = make_float2(oacc[j][2], oacc[j][3]);
-    }
-    if (tq == 0) {
-      *reinterpret_cast<float2*>(pml + r0 * 2) = make_float2(m0, l0);
-      *reinterpret_cast<float2*>(pml + r1 * 2) = make_float2(m1, l1);
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------
-// tcgen05 attention (Flash-Cache and Flash-Verify).  Same work items, key
-// slicing, split-KV partial format and results as attn_kernel, with the
-// products on the 5th-generation tensor cores: S = Q K^T and O += P V are
+// tcgen05 attention (Flash-Cache and Flash-Verify).  The products run on the
+// 5th-generation tensor cores: S = Q K^T and O += P V are
 // M=128 UMMAs issued by one thread, S (double-buffered) and the O accumulator
 // live in tensor memory, and only P passes through shared memory (bf16,
 // 128-byte swizzled: the A operand of the second product).  V is read in
@@ -509,7 +189,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 //   MMA:       S(t) -> s_full, k_empty;  then PV(t-1) after p_full(t-1) ->
 //              pv_done, v_empty
 //   softmax:   S(t) -> s_empty;  P(t) -> p_full once PV(t-2) freed the buffer
-//   scores:    S(t) rows of qbar -> s_empty, atomics
+//   scores:    S(t) rows of qbar -> s_empty, column sums to the workspace
 // ---------------------------------------------------------------------------
 constexpr int kTcWarps = 12;
 constexpr int kTcThreads = kTcWarps * 32;
@@ -677,7 +357,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int nt_blk = (kVerify && split == p.kv_splits - 1) ? (it.blk_rows + kKeyTile - 1) / kKeyTile : 0;
     n_tiles = nt_cache + nt_blk;
   }
-  const bool scores_on = !kVerify && has_item && p.scores != nullptr && it.m_len > 0;
+  const bool scores_on = !kVerify && has_item && p.colsum != nullptr && it.m_len > 0 && it.mchunk >= 0;
   const int64_t d = p.d_model;
   {
     // the CTA exits only when neither half has an item
@@ -738,7 +418,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int hh = tid >> 6, rr = F.qbar_lane + ((tid >> 3) & 7), ch = tid & 7;
       *reinterpret_cast<uint4*>(win_chunk(hh ? F.q_win1 : F.q_win0, rr, ch)) = make_uint4(0, 0, 0, 0);
     }
-    const bool f_scores = !kVerify && f_has && p.scores != nullptr && fi.m_len > 0;
+    const bool f_scores = !kVerify && f_has && p.colsum != nullptr && fi.m_len > 0 && fi.mchunk >= 0;
     if (f_scores) {
       // qbar dim = tid: fp32 sum over the masked rows (the item's first m_len
       // rows) -> bf16 hi (row qbar_lane) and lo (row qbar_lane + 1)
@@ -777,11 +457,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           *fail = 1;
           break;
         }
-        const int y = it.seq * p.seqlen_max + c0 + t * kKeyTile;
+        const int n0 = c0 + t * kKeyTile;  // a multiple of 64: one page
+        int64_t y = static_cast<int64_t>(it.seq) * p.seqlen_max + n0;
+        if (p.pages != nullptr) {
+          const int64_t page = p.pages[static_cast<int64_t>(it.seq) * p.pages_per_seq + n0 / kKeyTile];
+          if (page < 0 || (page + 1) * kKeyTile > p.n_slots) {
+            // a page outside the cache: recorded; the tile is read from row 0
+            // (in bounds) so the pipeline still completes
+            if (is_k) report(p.status, FDLLM_ERR_INDEX, static_cast<int>(page), kAttnKernelId);
+            y = 0;
+          } else {
+            y = page * kKeyTile;
+          }
+        }
         uint8_t* dst = (is_k ? H.k : H.v) + s * kTileBytes;
         mbar_arrive_expect_tx(&full[s], kTileBytes);
-        tma_load_2d(dst, map, head * kHD, y, &full[s]);
-        tma_load_2d(dst + kHalfBytes, map, head * kHD + 64, y, &full[s]);
+        tma_load_2d(dst, map, head * kHD, static_cast<int32_t>(y), &full[s]);
+        tma_load_2d(dst + kHalfBytes, map, head * kHD + 64, static_cast<int32_t>(y), &full[s]);
       }
     }
   } else if (role == kProdK || role == kProdV) {
@@ -923,7 +615,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (role == kScores) {
     // ------------------------------------------------------- scores ----
     if (scores_on) {
-      float* srow = p.scores + static_cast<int64_t>(it.seq) * p.seqlen_max;
+      // this (item, head)'s own row of column sums: written, never accumulated
+      float* srow = p.colsum + (static_cast<int64_t>(it.mchunk) * p.n_heads + head) *
+                                   static_cast<int64_t>(p.seqlen_max);
       const uint32_t taddr = tmem + (H.qbar_lane << 16);  // lanes qbar, qbar+1 = hi, lo
       for (int t = 0; t < n_tiles; ++t) {
         const int b = t & 1;
@@ -948,8 +642,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
         const int n0 = c0 + t * kKeyTile;
         const int n_valid = c1 - n0;
-        if (lane < n_valid) atomicAdd(srow + n0 + lane, H.scr[lane] * p.score_scale);
-        if (lane + 32 < n_valid) atomicAdd(srow + n0 + lane + 32, H.scr[lane + 32] * p.score_scale);
+        if (lane < n_valid) srow[n0 + lane] = H.scr[lane];
+        if (lane + 32 < n_valid) srow[n0 + lane + 32] = H.scr[lane + 32];
         __syncwarp();
       }
     }
@@ -1158,54 +852,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-// Merge split-KV partials: O = sum_s 2^(m_s - m) O_s / sum_s 2^(m_s - m) l_s.
-template <bool kVerify>
-__global__ void __launch_bounds__(256) attn_combine_kernel(const AttnParams p) {
-  const int item_id = blockIdx.x;
-  const int head = blockIdx.y;
-  Item it{};
-  if (!load_item(p, kVerify, item_id, it)) return;
-  const int64_t base = (static_cast<int64_t>(item_id) * p.n_heads + head) * p.kv_splits;
-  // work unit: row = w / 4, dims [(w%4)*32, +32)
-  for (int w = threadIdx.x; w < kItemRows * 4; w += blockDim.x) {
-    const int r = w >> 2;
-    if (r >= it.rows) continue;
-    const int d0 = (w & 3) * 32;
-    float mmax = -INFINITY;
-    for (int s = 0; s < p.kv_splits; ++s) mmax = fmaxf(mmax, p.part_ml[((base + s) * kItemRows + r) * 2]);
-    const float ref = mmax == -INFINITY ? 0.f : mmax;
-    float acc[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-    float lsum = 0.f;
-    for (int s = 0; s < p.kv_splits; ++s) {
-      const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + ((base + s) * kItemRows + r) * 2);
-      const float wgt = exp2f(ml.x - ref);
-      lsum += wgt * ml.y;
-      const float* po = p.part_o + ((base + s) * kItemRows + r) * kHD + d0;
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(po + i);
-        acc[i] += wgt * v.x;
-        acc[i + 1] += wgt * v.y;
-        acc[i + 2] += wgt * v.z;
-        acc[i + 3] += wgt * v.w;
-      }
-    }
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-    __nv_bfloat16* o = p.o + static_cast<int64_t>(item_row(it, r)) * p.d_model + head * kHD + d0;
-#pragma unroll
-    for (int i = 0; i < 32; i += 8) {
-      uint4 v;
-      v.x = pack_bf16x2(acc[i] * inv, acc[i + 1] * inv);
-      v.y = pack_bf16x2(acc[i + 2] * inv, acc[i + 3] * inv);
-      v.z = pack_bf16x2(acc[i + 4] * inv, acc[i + 5] * inv);
-      v.w = pack_bf16x2(acc[i + 6] * inv, acc[i + 7] * inv);
-      *reinterpret_cast<uint4*>(o + i) = v;
-    }
-  }
-}
-
 // ------------------------------------------------------------ planner ----
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanMaxBatch = 1024;
@@ -1217,7 +863,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* __res
                                                             int32_t* status) {
   __shared__ int m_start[kPlanMaxBatch], m_len[kPlanMaxBatch], m_cnt[kPlanMaxBatch];
   __shared__ int t_min[kPlanMaxBatch], t_max[kPlanMaxBatch], t_len[kPlanMaxBatch];
-  __shared__ int k_end[kPlanMaxBatch], n_it[kPlanMaxBatch], off[kPlanMaxBatch];
+  __shared__ int k_end[kPlanMaxBatch], n_it[kPlanMaxBatch], off[kPlanMaxBatch], moff[kPlanMaxBatch];
   __shared__ int bad;
   const int tid = threadIdx.x;
   if (tid == 0) bad = 0;
@@ -1259,17 +905,30 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* __res
     n_it[b] = rows > 0 ? (rows + kItemRows - 1) / kItemRows : 0;
   }
   __syncthreads();
+  const int seq_off = kPlanHeader + capacity * kPlanItem;
   if (tid == 0) {
-    int acc = 0;
+    int acc = 0, macc = 0;
     for (int b = 0; b < batch; ++b) {
       off[b] = acc;
       acc += n_it[b];
+      moff[b] = macc;
+      macc += (m_len[b] + kItemRows - 1) / kItemRows;
     }
     if (acc > capacity) bad = -1;
     plan[0] = bad != 0 ? 0 : acc;
+    plan[1] = batch;
+    plan[2] = bad != 0 ? 0 : macc;
+    plan[3] = seq_off;
     if (bad != 0) report(status, FDLLM_ERR_TABLE, bad, kPlanKernelId);
   }
   __syncthreads();
+  for (int b = tid; b < batch; b += kPlanThreads) {
+    int32_t* e = plan + seq_off + kPlanSeq * b;
+    const bool live = bad == 0 && m_len[b] + t_len[b] > 0;
+    e[0] = live ? moff[b] : 0;
+    e[1] = live ? (m_len[b] + kItemRows - 1) / kItemRows : 0;
+    e[2] = live ? k_end[b] : 0;
+  }
   if (bad != 0) return;
   for (int b = tid; b < batch; b += kPlanThreads) {
     const int rows = m_len[b] + t_len[b];
@@ -1284,51 +943,61 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* __res
       e[3] = mseg;
       e[4] = t_len[b] > 0 ? t_min[b] + (tfrom - m_len[b]) : 0;
       e[5] = max(0, v1 - tfrom);
-      e[6] = 0;
+      e[6] = mseg > 0 ? moff[b] + k : -1;
       e[7] = 0;
     }
   }
+}
+
+// ------------------------------------------------- score reduction ----
+// attn_scores[b * seqlen_max + n] += score_scale * (sum over the masked items
+// of sequence b, in item order, of the sum over heads, in head order, of the
+// column sums the attention kernel wrote).  One thread per key; a fixed
+// order, so the result does not depend on which CTAs finished first.
+// ref llada/flash_cache_triton.py:614-615 (attn_scores += S.mean((0, 1))).
+constexpr int kScoreThreads = 256;
+
+__global__ void __launch_bounds__(kScoreThreads)
+    scores_reduce_kernel(const int32_t* __restrict__ plan, const float* __restrict__ colsum,
+                         float* __restrict__ scores, float score_scale, int n_heads, int seqlen_max) {
+  pdl_wait();  // the column sums come from the attention kernel before
+  const int b = blockIdx.y;
+  if (b >= plan[1]) return;
+  const int32_t* sq = plan + plan[3] + kPlanSeq * b;
+  const int first = sq[0], n_masked = sq[1], k_end = sq[2];
+  const int key = blockIdx.x * kScoreThreads + threadIdx.x;
+  if (n_masked <= 0 || key >= k_end) return;
+  const int64_t ld = seqlen_max;
+  const float* c = colsum + static_cast<int64_t>(first) * n_heads * ld + key;
+  float acc = 0.f;
+  for (int m = 0; m < n_masked; ++m)
+    for (int h = 0; h < n_heads; ++h) acc += c[(static_cast<int64_t>(m) * n_heads + h) * ld];
+  scores[static_cast<int64_t>(b) * ld + key] += acc * score_scale;
 }
 
 namespace {
 
 int plan_capacity(int32_t n_rows, int32_t batch) { return (n_rows + kItemRows - 1) / kItemRows + batch; }
 
-// Workspace layout when keys are split (mma.sync kernel: its combine kernel
-// reads them; the tcgen05 kernel merges in distributed shared memory): the
-// partial O rows, then the partial (m, l).
-size_t attn_ws_bytes(int32_t items, int32_t heads, int32_t splits) {
-  if (splits <= 1) return 256;
-  const size_t slots = static_cast<size_t>(items) * heads * splits;
-  return align_up(slots * kItemRows * kHD * sizeof(float), 256) + slots * kItemRows * 2 * sizeof(float);
+// Workspace of fdllm_attn_cache with scores: one row of column sums per
+// (masked item, head); the masked items are at most the plan's capacity.
+size_t attn_ws_bytes(int32_t items, int32_t heads, int32_t seqlen_max) {
+  if (items <= 0 || heads <= 0 || seqlen_max <= 0) return 256;
+  return align_up(static_cast<size_t>(items) * heads * seqlen_max * sizeof(float), 256);
 }
 
 // Key splits the tcgen05 kernel runs: its cluster merge takes 1, 2, 4 or 8
 // (a request in between rounds down; results do not depend on the split).
 int tc_splits(int requested) { return requested >= 8 ? 8 : requested >= 4 ? 4 : requested >= 2 ? 2 : 1; }
 
-// Attention runs on the tcgen05 kernel; FDLLM_ATTN_MMA_SYNC=1 selects the
-// mma.sync kernel instead (kept as the comparison point).
-bool use_tc_attention() {
-  static const bool tc = env_int("FDLLM_ATTN_MMA_SYNC", 0) == 0;
-  return tc;
-}
-
 template <bool kVerify>
 int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mk1, const CUtensorMap& mv1,
-                AttnParams& p, int grid_items, void* ws, size_t ws_bytes, cudaStream_t stream) {
+                AttnParams& p, int grid_items, cudaStream_t stream) {
   static bool attr[64] = {false};
-  const bool tc = use_tc_attention();
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr[dev]) {
-    // Two CTAs per SM need the largest shared-memory carveout; the driver's
-    // default split can leave room for one only.
-    if (cudaFuncSetAttribute(attn_kernel<kVerify>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(attn_kernel<kVerify>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-      return FDLLM_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return FDLLM_ERR_ARG;
+  if (!attr[dev]) {
     if (cudaFuncSetAttribute(attn_tc_kernel<kVerify>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) !=
             cudaSuccess ||
         cudaFuncSetAttribute(attn_tc_kernel<kVerify>, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -1336,28 +1005,13 @@ int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap&
       return FDLLM_ERR_CUDA;
     attr[dev] = true;
   }
-  if (tc) {
-    // one CTA = two work items; key splits as clusters of CTAs
-    p.kv_splits = tc_splits(p.kv_splits);
-    const dim3 grid(static_cast<unsigned>((grid_items + 1) / 2 * p.kv_splits), static_cast<unsigned>(p.n_heads), 1);
-    if (launch_ex(attn_tc_kernel<kVerify>, grid, dim3(kTcThreads), kTcSmem, stream,
-                  static_cast<unsigned>(p.kv_splits), pdl_enabled(), mk, mv, mk1, mv1, p) != cudaSuccess)
-      return FDLLM_ERR_CUDA;
-    return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
-  }
-  if (p.kv_splits > 1) {
-    if (ws == nullptr || ws_bytes < attn_ws_bytes(grid_items, p.n_heads, p.kv_splits)) return FDLLM_ERR_WORKSPACE;
-    const size_t slots = static_cast<size_t>(grid_items) * p.n_heads * p.kv_splits;
-    p.part_o = static_cast<float*>(ws);
-    p.part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align_up(slots * kItemRows * kHD * sizeof(float), 256));
-  }
-  attn_kernel<kVerify><<<dim3(grid_items, p.n_heads, p.kv_splits), kAttnThreads, kAttnSmem, stream>>>(mk, mv, p);
-  if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
-  if (p.kv_splits > 1) {
-    attn_combine_kernel<kVerify><<<dim3(grid_items, p.n_heads), 256, 0, stream>>>(p);
-    if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
-  }
-  return FDLLM_OK;
+  // one CTA = two work items; key splits as clusters of CTAs
+  p.kv_splits = tc_splits(p.kv_splits);
+  const dim3 grid(static_cast<unsigned>((grid_items + 1) / 2 * p.kv_splits), static_cast<unsigned>(p.n_heads), 1);
+  if (launch_ex(attn_tc_kernel<kVerify>, grid, dim3(kTcThreads), kTcSmem, stream, static_cast<unsigned>(p.kv_splits),
+                pdl_enabled(), mk, mv, mk1, mv1, p) != cudaSuccess)
+    return FDLLM_ERR_CUDA;
+  return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
 }
 
 }  // namespace
@@ -1371,7 +1025,9 @@ int fdllm_attn_plan_capacity(int32_t n_rows, int32_t batch_size) {
 
 size_t fdllm_attn_plan_bytes(int32_t n_rows, int32_t batch_size) {
   const int cap = fdllm_attn_plan_capacity(n_rows, batch_size);
-  return sizeof(int32_t) * (fdllm::kPlanHeader + static_cast<size_t>(cap) * fdllm::kPlanItem);
+  const size_t batch = batch_size < 0 ? 0 : static_cast<size_t>(batch_size);
+  return sizeof(int32_t) *
+         (fdllm::kPlanHeader + static_cast<size_t>(cap) * fdllm::kPlanItem + batch * fdllm::kPlanSeq);
 }
 
 int fdllm_plan_cache_attention(const int64_t* masked_blocks, int32_t n_masked, const int64_t* tracked_blocks,
@@ -1389,22 +1045,29 @@ int fdllm_plan_cache_attention(const int64_t* masked_blocks, int32_t n_masked, c
   return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
 }
 
-size_t fdllm_attn_workspace_bytes(int32_t max_items, int32_t n_heads, int32_t kv_splits) {
-  return fdllm::attn_ws_bytes(max_items, n_heads, kv_splits);
+size_t fdllm_attn_workspace_bytes(int32_t max_items, int32_t n_heads, int32_t seqlen_max) {
+  return fdllm::attn_ws_bytes(max_items, n_heads, seqlen_max);
 }
 
 int fdllm_attn_cache(const void* q, void* o, const void* k_cache, const void* v_cache, const void* plan,
                      int32_t max_items, float* attn_scores, float score_scale, int32_t d_model, int32_t n_heads,
-                     int32_t seqlen_max, int64_t n_slots, float softmax_scale, int32_t kv_splits, void* workspace,
-                     size_t workspace_bytes, cudaStream_t stream) {
+                     int32_t seqlen_max, int64_t n_slots, float softmax_scale, int32_t kv_splits,
+                     const int32_t* page_table, int32_t pages_per_seq, void* workspace, size_t workspace_bytes,
+                     cudaStream_t stream) {
   using namespace fdllm;
   if (n_heads <= 0 || d_model != n_heads * kHD || seqlen_max <= 0 || n_slots <= 0 || max_items < 0 ||
       kv_splits < 1 || kv_splits > 64)
+    return FDLLM_ERR_ARG;
+  if (page_table != nullptr &&
+      (pages_per_seq <= 0 || static_cast<int64_t>(pages_per_seq) * kKeyTile < seqlen_max || n_slots < kKeyTile))
     return FDLLM_ERR_ARG;
   if (max_items == 0) return FDLLM_OK;
   const void* ptrs[] = {q, o, k_cache, v_cache, plan};
   for (const void* x : ptrs)
     if (x == nullptr || !aligned16(x)) return FDLLM_ERR_ARG;
+  if (attn_scores != nullptr &&
+      (workspace == nullptr || workspace_bytes < attn_ws_bytes(max_items, n_heads, seqlen_max)))
+    return FDLLM_ERR_WORKSPACE;
   CUtensorMap mk, mv;
   int rc;
   if ((rc = make_tmap_bf16_sw128(&mk, k_cache, n_slots, d_model, d_model, kKeyTile)) != FDLLM_OK) return rc;
@@ -1415,7 +1078,9 @@ int fdllm_attn_cache(const void* q, void* o, const void* k_cache, const void* v_
   p.kc = static_cast<const __nv_bfloat16*>(k_cache);
   p.vc = static_cast<const __nv_bfloat16*>(v_cache);
   p.plan = static_cast<const int32_t*>(plan);
-  p.scores = attn_scores;
+  p.colsum = attn_scores != nullptr ? static_cast<float*>(workspace) : nullptr;
+  p.pages = page_table;
+  p.pages_per_seq = page_table != nullptr ? pages_per_seq : 0;
   p.status = status_ptr();
   p.n_slots = n_slots;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
@@ -1424,7 +1089,14 @@ int fdllm_attn_cache(const void* q, void* o, const void* k_cache, const void* v_
   p.n_heads = n_heads;
   p.seqlen_max = seqlen_max;
   p.kv_splits = kv_splits;
-  return launch_attn<false>(mk, mv, mk, mv, p, max_items, workspace, workspace_bytes, stream);
+  if ((rc = launch_attn<false>(mk, mv, mk, mv, p, max_items, stream)) != FDLLM_OK) return rc;
+  if (attn_scores == nullptr) return FDLLM_OK;
+  const dim3 sgrid(static_cast<unsigned>((seqlen_max + kScoreThreads - 1) / kScoreThreads),
+                   static_cast<unsigned>(max_items), 1);
+  if (launch_ex(scores_reduce_kernel, sgrid, dim3(kScoreThreads), 0, stream, 1, pdl_enabled(), p.plan,
+                static_cast<const float*>(p.colsum), attn_scores, score_scale, n_heads, seqlen_max) != cudaSuccess)
+    return FDLLM_ERR_CUDA;
+  return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
 }
 
 int fdllm_verify_attn(const void* q1, const void* k1, const void* v1, void* o, const void* k_cache,
@@ -1471,7 +1143,9 @@ int fdllm_verify_attn(const void* q1, const void* k1, const void* v1, void* o, c
   if ((rc = make_tmap_bf16_sw128(&mv, v_cache, n_slots, d_model, d_model, kKeyTile)) != FDLLM_OK) return rc;
   if ((rc = make_tmap_bf16_sw128(&mk1, k1, n_rows, d_model, d_model, kKeyTile)) != FDLLM_OK) return rc;
   if ((rc = make_tmap_bf16_sw128(&mv1, v1, n_rows, d_model, d_model, kKeyTile)) != FDLLM_OK) return rc;
-  return launch_attn<true>(mk, mv, mk1, mv1, p, p.n_items, workspace, workspace_bytes, stream);
+  (void)workspace;  // reserved: the verify kernel needs no workspace
+  (void)workspace_bytes;
+  return launch_attn<true>(mk, mv, mk1, mv1, p, p.n_items, stream);
 }
 
 }  // extern "C"

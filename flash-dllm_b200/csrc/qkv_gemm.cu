@@ -877,15 +877,28 @@ struct QkvPlan {
   bool pair;  // CTA-pair stream-K kernel (more than 128 rows)
 };
 
+// Plan overrides for tuning and tests (fdllm_qkv_set_plan); 0 / -1 mean
+// automatic.  The first values come from FDLLM_QKV_BN / FDLLM_QKV_SPLITS /
+// FDLLM_QKV_KSUB / FDLLM_QKV_PAIR, read once per process.
+struct QkvOverride {
+  int bn, splits, ksub, pair;
+};
+
+QkvOverride& qkv_override() {
+  static QkvOverride o{env_int("FDLLM_QKV_BN", 0), env_int("FDLLM_QKV_SPLITS", 1), env_int("FDLLM_QKV_KSUB", 0),
+                       env_int("FDLLM_QKV_PAIR", -1)};
+  return o;
+}
+
 // Units are spread round-robin over one CTA per SM.  Tiles are 128 columns
 // (one head) wide and K is not split by default: at 64 and 128 rows (96
 // tiles) whole-K tiles on 96 SMs measured faster than 64-wide tiles on all
 // SMs (64 rows: 35.5 vs 39.6 us) and than 2-6 K splits, whose fp32 partials
-// cost more than the balance gains (64 rows: 41.7-92 us).  FDLLM_QKV_BN /
-// FDLLM_QKV_SPLITS / FDLLM_QKV_KSUB override the choices.
+// cost more than the balance gains (64 rows: 41.7-92 us).
 QkvPlan plan_qkv(int32_t n_rows, int32_t d_model, int32_t n_heads) {
   QkvPlan pl{};
-  int ksub = env_int("FDLLM_QKV_KSUB", 0);
+  const QkvOverride& ov = qkv_override();
+  int ksub = ov.ksub;
   if (ksub != 1 && ksub != 2) ksub = 2;
   if (d_model % (kQkvBK * ksub) != 0) ksub = 1;
   pl.ksub = ksub;
@@ -893,12 +906,12 @@ QkvPlan plan_qkv(int32_t n_rows, int32_t d_model, int32_t n_heads) {
   const int sms = sm_count();
   pl.m_tiles = (n_rows + kQkvBM - 1) / kQkvBM;
   pl.xrows = n_rows <= 64 ? 64 : 128;
-  int bn = env_int("FDLLM_QKV_BN", 0);
+  int bn = ov.bn;
   if (bn != 64 && bn != 128) bn = 128;
   pl.bn = bn;
   pl.n_tiles = 3 * n_heads * (128 / bn);
   const int tiles = pl.m_tiles * pl.n_tiles;
-  int splits = env_int("FDLLM_QKV_SPLITS", 1);
+  int splits = ov.splits;
   if (splits < 1) splits = 1;
   if (splits > kb_total) splits = kb_total;
   pl.kb_per_split = (kb_total + splits - 1) / splits;
@@ -908,7 +921,7 @@ QkvPlan plan_qkv(int32_t n_rows, int32_t d_model, int32_t n_heads) {
   // CTA pairs for 129-256 rows, where they measured faster (256 rows: 45.9
   // vs 51.1 us; 384 and 512 rows: 69 vs 55-66 us).  FDLLM_QKV_PAIR=1 / 0
   // forces them on above 128 rows / off.
-  const int pair_env = env_int("FDLLM_QKV_PAIR", -1);
+  const int pair_env = ov.pair;
   pl.pair = n_rows > 128 && d_model % kQkvBK == 0 && (pair_env < 0 ? n_rows <= 256 : pair_env != 0);
   if (pl.pair) {
     pl.splits = 1;
@@ -1047,6 +1060,18 @@ int launch_qkv(const void* xn, const void* wq, const void* wk, const void* wv, c
 
 extern "C" {
 
+int fdllm_qkv_set_plan(int32_t bn, int32_t splits, int32_t ksub, int32_t pair) {
+  if ((bn != 0 && bn != 64 && bn != 128) || splits < 0 || (ksub != 0 && ksub != 1 && ksub != 2) || pair < -1 ||
+      pair > 1)
+    return FDLLM_ERR_ARG;
+  fdllm::QkvOverride& o = fdllm::qkv_override();
+  o.bn = bn;
+  o.splits = splits < 1 ? 1 : splits;
+  o.ksub = ksub;
+  o.pair = pair;
+  return FDLLM_OK;
+}
+
 size_t fdllm_qkv_workspace_bytes(int32_t n_rows, int32_t d_model, int32_t n_heads) {
   if (n_rows <= 0 || n_heads <= 0 || d_model != n_heads * 128) return 256;
   return fdllm::qkv_ws_bytes(fdllm::plan_qkv(n_rows, d_model, n_heads));
@@ -1090,9 +1115,11 @@ int fdllm_verify_qkv(const void* xn, const void* wq, const void* wk, const void*
 //  * The first call on a device resolves the array's device address
 //    (cudaGetSymbolAddress, with that device current); make that first call
 //    before any stream capture.
-//  * All calls share the array: the split counters are cleared at the start
-//    of every call, and calls that overlap on the GPU (other streams, other
-//    threads) race on it -- serialise them.
+//  * All calls share the array: its counter / flag region (split-K tile
+//    counters, CTA-pair handoff flags) is zeroed on entry of every call that
+//    uses the array, so a call that ended on a device error leaves nothing
+//    behind for the next one; calls that overlap on the GPU (other streams,
+//    other threads) race on it -- serialise them.
 //  * No cudaMalloc / cudaFree or other allocating routine is called.
 // ---------------------------------------------------------------------------
 namespace {
@@ -1125,7 +1152,12 @@ extern "C" int fdllm_qkv_rope_cache_noalloc(const void* xn, const void* wq, cons
   if ((pl.splits > 1 || pl.pair) && qkv_ws_bytes(pl) > kQkvNoAllocScratchBytes) return FDLLM_ERR_SCRATCH_LIMIT;
   void* scratch = qkv_noalloc_scratch();
   if (scratch == nullptr) return FDLLM_ERR_CUDA;
-  if (pl.splits > 1 && cudaMemsetAsync(scratch, 0, kQkvCounterBytes, stream) != cudaSuccess) return FDLLM_ERR_CUDA;
+  // The counter / flag region at the front of the array is zeroed before
+  // every call that uses the array: a call that ended on a device error may
+  // have left split-K tile counters or CTA-pair handoff flags set, and this
+  // caller has no other way to clear them.
+  if ((pl.splits > 1 || pl.pair) && cudaMemsetAsync(scratch, 0, kQkvCounterBytes, stream) != cudaSuccess)
+    return FDLLM_ERR_CUDA;
   return launch_qkv(xn, wq, wk, wv, pos, rope_sin, rope_cos, q_out, k_cache, v_cache, n_rows, d_model, n_heads,
                     n_slots, scratch, kQkvNoAllocScratchBytes, 1, stream);
 }

@@ -41,23 +41,30 @@ def _eps(module) -> float:
 
 
 class _PlanCache:
-    """The attention plan of one forward pass: every layer of a forward gets
-    the same block-table tensor objects, so the plan is built at the first
-    layer and reused by the others (the tensors are held, so their identity
-    cannot be recycled while cached)."""
+    """The attention plan of one forward pass, one entry per device: every
+    layer of a forward gets the same block-table tensor objects, so the plan
+    is built at the first layer and reused by the others.  An entry matches
+    only the same tensor objects (held, so their identity cannot be recycled
+    while cached) at the same version counter (an in-place edit of a table
+    bumps it and forces a new plan), and the same sizes."""
 
     def __init__(self):
-        self.key = None
-        self.value = None
+        self.entries = {}
+
+    @staticmethod
+    def _key(masked, tracked, n_rows, batch, block_m, max_length):
+        ver = tuple(None if t is None else t._version for t in (masked, tracked))
+        return (masked, tracked, ver, n_rows, batch, block_m, max_length)
 
     def get(self, masked, tracked, n_rows, batch, block_m, max_length, device):
-        key = (masked, tracked, n_rows, batch, block_m, max_length, device)
-        if self.key is not None and all(a is b if isinstance(a, torch.Tensor) else a == b
-                                        for a, b in zip(self.key, key)):
-            return self.value
-        self.value = ops.plan_cache_attention(masked, tracked, n_rows, batch, block_m, max_length, device)
-        self.key = key
-        return self.value
+        dev = device.index if device.index is not None else torch.cuda.current_device()
+        key = self._key(masked, tracked, n_rows, batch, block_m, max_length)
+        hit = self.entries.get(dev)
+        if hit is not None and all(a is b if isinstance(a, torch.Tensor) else a == b for a, b in zip(hit[0], key)):
+            return hit[1]
+        value = ops.plan_cache_attention(masked, tracked, n_rows, batch, block_m, max_length, device)
+        self.entries[dev] = (key, value)
+        return value
 
 
 _PLANS = _PlanCache()

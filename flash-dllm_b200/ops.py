@@ -48,6 +48,22 @@ class Workspace:
         cls._bufs.clear()
         cls._retired.clear()
 
+    @classmethod
+    def rezero(cls) -> None:
+        """Zero every live buffer in place (after a device error left
+        counters or flags set); addresses are kept."""
+        for buf in cls._bufs.values():
+            buf.zero_()
+
+
+_lib.on_device_error(Workspace.rezero)
+
+
+def set_qkv_plan(bn: int = 0, splits: int = 0, ksub: int = 0, pair: int = -1) -> None:
+    """Override the QKV kernel's plan (tuning and tests); no arguments
+    restore the automatic plan."""
+    call("fdllm_qkv_set_plan", bn, splits, ksub, pair)
+
 
 def _check(t: torch.Tensor, name: str, dtype=None, dim=None) -> None:
     if not t.is_cuda:
@@ -178,22 +194,32 @@ def plan_cache_attention(masked_blocks, tracked_blocks, n_rows: int, batch_size:
 
 def attn_cache(q, o, k_cache, v_cache, plan: torch.Tensor, capacity: int, attn_scores, score_scale: float,
                n_heads: int, seqlen_max: int, softmax_scale: float, kv_splits: int = 0,
-               items_hint: int = 0) -> None:
+               items_hint: int = 0, page_table: Optional[torch.Tensor] = None) -> None:
     """Masked + tracked attention over the cache, optional fused score
     accumulation.  ``items_hint`` estimates the plan's real item count (the
-    capacity is an upper bound) for the automatic key split."""
+    capacity is an upper bound) for the automatic key split.  ``page_table``
+    (int32 [batch, pages_per_seq]) maps key n of sequence b to cache row
+    ``page_table[b, n // 64] * 64 + n % 64``; without it sequence b owns rows
+    ``[b * seqlen_max, b * seqlen_max + k_end)``."""
     for t, n in ((q, "q"), (o, "o"), (k_cache, "k_cache"), (v_cache, "v_cache")):
         _check(t, n, BF16, 2)
     if attn_scores is not None:
         _check(attn_scores, "attn_scores", torch.float32)
+    pps = 0
+    if page_table is not None:
+        _check(page_table, "page_table", torch.int32, 2)
+        pps = page_table.shape[1]
     d_model = q.shape[1]
     if kv_splits <= 0:
         kv_splits = auto_kv_splits(items_hint if items_hint > 0 else capacity, n_heads, seqlen_max, q.device)
-    nbytes = _lib.lib().fdllm_attn_workspace_bytes(capacity, n_heads, kv_splits)
-    ws = Workspace.get(q.device, nbytes, "attn")
+    ws, nws = None, 0
+    if attn_scores is not None:
+        nbytes = _lib.lib().fdllm_attn_workspace_bytes(capacity, n_heads, seqlen_max)
+        ws = Workspace.get(q.device, nbytes, "attn")
+        nws = ws.numel()
     call("fdllm_attn_cache", ptr(q), ptr(o), ptr(k_cache), ptr(v_cache), ptr(plan), capacity, ptr(attn_scores),
          float(score_scale), d_model, n_heads, seqlen_max, k_cache.shape[0], float(softmax_scale), kv_splits,
-         ptr(ws), ws.numel(), _stream())
+         ptr(page_table), pps, ptr(ws), nws, _stream())
 
 
 def verify_attn(q1, k1, v1, o, k_cache, v_cache, pos_k, attn_mask, verify_blocks, block_rows: int, n_heads: int,
@@ -218,11 +244,9 @@ def verify_attn(q1, k1, v1, o, k_cache, v_cache, pos_k, attn_mask, verify_blocks
     items = nb * ((block_rows + 63) // 64)
     if kv_splits <= 0:
         kv_splits = auto_kv_splits(items, n_heads, max_keys if max_keys is not None else n_pos // nb, q1.device)
-    nbytes = _lib.lib().fdllm_attn_workspace_bytes(items, n_heads, kv_splits)
-    ws = Workspace.get(q1.device, nbytes, "attn")
     call("fdllm_verify_attn", ptr(q1), ptr(k1), ptr(v1), ptr(o), ptr(k_cache), ptr(v_cache), ptr(pos_k), n_pos,
          ptr(mask), ptr(vb), nb, block_rows, q1.shape[0], d_model, n_heads, k_cache.shape[0], float(softmax_scale),
-         kv_splits, ptr(ws), ws.numel(), _stream())
+         kv_splits, None, 0, _stream())
 
 
 # ------------------------------------------------------------- decoding --

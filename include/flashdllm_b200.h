@@ -13,9 +13,9 @@
  * Tensors are row-major and contiguous unless a leading dimension is given.
  * "bf16" means __nv_bfloat16 / torch.bfloat16.  The library allocates no
  * device memory: callers pass workspaces sized by the *_workspace_bytes()
- * queries (zero-filled once before first use; the kernels leave them ready
- * for the next call, except after a call whose device status reported an
- * error: zero the workspace again before reusing it).
+ * queries.  A QKV workspace is zero-filled once before first use and the
+ * kernels leave it ready for the next call, except after a call whose device
+ * status reported an error: zero it again before reusing it.
  *
  * Citations "ref file:line" name the reference interface each entry point
  * replaces (VILA-Lab/Flash-dLLM).
@@ -71,6 +71,14 @@ int fdllm_add_rmsnorm(const void* x, const void* residual, const void* weight, v
 int fdllm_swiglu(const void* gate, const void* up, void* out, int64_t rows, int32_t cols, int64_t ld_in,
                  cudaStream_t stream);
 
+/* Override the QKV kernel's plan (tuning and tests; not thread-safe against concurrent calls):
+ * bn = tile width 64 or 128 columns (0: automatic), splits = K splits (0 or 1: none), ksub = 64-wide
+ * K sub-tiles per ring slot 1 or 2 (0: automatic), pair = CTA-pair kernel above 128 rows: 1 on,
+ * 0 off, -1 automatic.  The initial values come from the FDLLM_QKV_BN / _SPLITS / _KSUB / _PAIR
+ * environment variables, read once.  The workspace query follows the current plan.  No reference
+ * counterpart (the reference's tile sizes are Triton constexprs). */
+int fdllm_qkv_set_plan(int32_t bn, int32_t splits, int32_t ksub, int32_t pair);
+
 /* Workspace (bytes) fdllm_qkv_rope_cache / fdllm_verify_qkv need for n_rows query rows. */
 size_t fdllm_qkv_workspace_bytes(int32_t n_rows, int32_t d_model, int32_t n_heads);
 
@@ -97,8 +105,9 @@ int fdllm_qkv_rope_cache(const void* xn, const void* wq, const void* wk, const v
  * rows with a requested K split) return FDLLM_ERR_SCRATCH_LIMIT without launching; the partial
  * sums of the CTA-pair kernel (129-256 rows, one 128 KB slot per CTA) fit.  The first call on a
  * device looks up the array's address; make it before any stream capture.  Calls share the
- * array (split-K counters are cleared on entry; the CTA-pair kernel leaves its flags at zero),
- * so calls that overlap on the GPU race: serialise them.  Allocates nothing. */
+ * array; its counter / flag region (split-K tile counters, CTA-pair handoff flags) is zeroed on
+ * entry of every call that uses it, so a call that ended on a device error leaves nothing stale
+ * behind.  Calls that overlap on the GPU race on the array: serialise them.  Allocates nothing. */
 int fdllm_qkv_rope_cache_noalloc(const void* xn, const void* wq, const void* wk, const void* wv, const int64_t* pos,
                                  const float* rope_sin, const float* rope_cos, void* q_out, void* k_cache,
                                  void* v_cache, int32_t n_rows, int32_t d_model, int32_t n_heads, int64_t n_slots,
@@ -113,7 +122,8 @@ int fdllm_verify_qkv(const void* xn, const void* wq, const void* wk, const void*
                      size_t workspace_bytes, cudaStream_t stream);
 
 /* Work-item capacity of an attention plan for n_rows query rows of batch_size sequences
- * (ceil(n_rows/64) + batch_size), and its size in bytes. */
+ * (ceil(n_rows/64) + batch_size), and its size in bytes (header, items, and a per-sequence
+ * section the score reduction reads). */
 int fdllm_attn_plan_capacity(int32_t n_rows, int32_t batch_size);
 size_t fdllm_attn_plan_bytes(int32_t n_rows, int32_t batch_size);
 
@@ -130,31 +140,41 @@ int fdllm_plan_cache_attention(const int64_t* masked_blocks, int32_t n_masked, c
                                int32_t n_tracked, int32_t n_rows, int32_t batch_size, int32_t block_m,
                                int32_t seqlen_max, void* plan, size_t plan_bytes, cudaStream_t stream);
 
-/* Workspace (bytes) for fdllm_attn_cache / fdllm_verify_attn with the given item count and split count. */
-size_t fdllm_attn_workspace_bytes(int32_t max_items, int32_t n_heads, int32_t kv_splits);
+/* Workspace (bytes) fdllm_attn_cache needs when it accumulates attn_scores: one fp32 row of
+ * seqlen_max column sums per (masked work item, head), max_items = fdllm_attn_plan_capacity(...).
+ * Needs no zero-fill: every value read is written by the same call. */
+size_t fdllm_attn_workspace_bytes(int32_t max_items, int32_t n_heads, int32_t seqlen_max);
 
 /* Block-table scheduled attention over the KV cache for masked + tracked rows.
  *   q          bf16 [n_rows, d_model];  o  bf16 [n_rows, d_model]
- *   k_cache, v_cache  bf16 [n_slots, d_model]; sequence b owns slots [b*seqlen_max, b*seqlen_max+k_end)
+ *   k_cache, v_cache  bf16 [n_slots, d_model].  Without a page table, sequence b owns rows
+ *              [b*seqlen_max, b*seqlen_max + k_end) (the reference's layout).  With one
+ *              (page_table int32 [batch, pages_per_seq], pages_per_seq * 64 >= seqlen_max), key n
+ *              of sequence b is row page_table[b*pages_per_seq + n/64]*64 + n%64; a page outside
+ *              the cache is reported as FDLLM_ERR_INDEX and read as row 0.
  *   plan       from fdllm_plan_cache_attention; max_items = fdllm_attn_plan_capacity(...)
- *   attn_scores  fp32 [batch*seqlen_max] or NULL: when given, for every key n of sequence b
- *              attn_scores[b*seqlen_max + n] += score_scale * sum over masked rows and heads of the
- *              raw (unscaled) q.k logit -- the reference's S tensor + S.mean((0,1)) fused.
- *   kv_splits  split of each item's key range over CTAs: 1 = none; the tcgen05 kernel runs 2, 4 or 8
- *              (other counts round down) as one cluster of CTAs per item pair, merged in distributed
- *              shared memory; the workspace holds partials only for the mma.sync comparison kernel
+ *   attn_scores  fp32 [batch*seqlen_max] (logical slots) or NULL: when given, for every key n of
+ *              sequence b, attn_scores[b*seqlen_max + n] += score_scale * sum over masked rows and
+ *              heads of the raw (unscaled) q.k logit -- the reference's S tensor + S.mean((0,1))
+ *              fused.  The sum is taken in a fixed order (a second kernel adds per-head column sums
+ *              from the workspace), so the scores are the same on every run.
+ *   kv_splits  split of each item's key range over CTAs: 1 = none; 2, 4 or 8 (other counts round
+ *              down) run as one cluster of CTAs per item pair, merged in distributed shared memory
  * ref llada/flash_cache_triton.py:103-252 (_flash_masked_attention_fwd, _flash_tracked_attention_fwd)
- * and :538, :614-615 (S and attn_scores). */
+ * and :538, :614-615 (S and attn_scores); the page table has no reference counterpart (the reference
+ * addresses start_n = batch_id * SEQLEN_MAX, :122 and :202). */
 int fdllm_attn_cache(const void* q, void* o, const void* k_cache, const void* v_cache, const void* plan,
                      int32_t max_items, float* attn_scores, float score_scale, int32_t d_model, int32_t n_heads,
-                     int32_t seqlen_max, int64_t n_slots, float softmax_scale, int32_t kv_splits, void* workspace,
-                     size_t workspace_bytes, cudaStream_t stream);
+                     int32_t seqlen_max, int64_t n_slots, float softmax_scale, int32_t kv_splits,
+                     const int32_t* page_table, int32_t pages_per_seq, void* workspace, size_t workspace_bytes,
+                     cudaStream_t stream);
 
 /* Flash-Verify attention: rows [q_s, q_e) of verify block row b = (k_s, k_e, q_s, q_e) (int32
  * [n_blocks, 4]) attend to cache rows pos_k[k_s:k_e] (gathered) and to their own block's fresh
  * k1/v1 rows under attn_mask (bool/uint8 [n_blocks*block_rows, block_rows]); block_rows = 2*block_m.
  * The in-block part is merged with a re-stabilised online softmax (the reference reuses the
- * cache part's running max, which yields NaN rows when a sequence has no cache keys).
+ * cache part's running max, which yields NaN rows when a sequence has no cache keys).  kv_splits
+ * as for fdllm_attn_cache; workspace / workspace_bytes are reserved (may be NULL / 0).
  * ref llada/flash_cache_triton.py:341-428 (_flash_verify_attention_fwd) and its launch at :521-535. */
 int fdllm_verify_attn(const void* q1, const void* k1, const void* v1, void* o, const void* k_cache,
                       const void* v_cache, const int64_t* pos_k, int64_t n_pos_k, const uint8_t* attn_mask,

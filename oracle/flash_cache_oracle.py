@@ -159,6 +159,22 @@ def cache_attention(q, o, k_cache, v_cache, block_table, seqlen_max: int, n_head
         o[idx] = st.finish().reshape(len(idx), -1).to(o.dtype)
 
 
+def pages_to_contiguous(cache: torch.Tensor, page_table: torch.Tensor, seqlen_max: int,
+                        page: int = 64) -> torch.Tensor:
+    """Gather a paged cache back into the reference's contiguous layout.
+
+    Key ``n`` of sequence ``b`` lives at row ``page_table[b, n // page] * page
+    + n % page`` of ``cache``; the result holds it at row ``b * seqlen_max +
+    n``, which is where ``cache_attention`` (the reference kernels,
+    ``start_n = batch_id * SEQLEN_MAX``, flash_cache_triton.py:122, 202) reads
+    it.  The reference has no page table; this is the oracle of the paged
+    variant."""
+    B = page_table.shape[0]
+    n = torch.arange(seqlen_max)
+    rows = page_table.long()[:, n // page] * page + (n % page)[None, :]
+    return cache[rows.reshape(-1)].reshape(B * seqlen_max, cache.shape[1])
+
+
 def verify_attention(q1, k1, v1, o, k_cache, v_cache, pos_k, attn_mask, block_table,
                      n_heads: int, block_m: int, softmax_scale: float, block_n: int = 64) -> None:
     """K5 ``_flash_verify_attention_fwd`` (flash_cache_triton.py:341-428).

@@ -23,3 +23,12 @@ def pytest_collection_modifyitems(config, items):
     for it in items:
         if "gpu" in it.keywords:
             it.add_marker(skip)
+
+
+@pytest.fixture
+def qkv_plan():
+    """Set a QKV plan override for one test (``qkv_plan(splits=3)``); the
+    automatic plan is restored afterwards."""
+    from flash_dllm_b200 import ops
+    yield ops.set_qkv_plan
+    ops.set_qkv_plan()

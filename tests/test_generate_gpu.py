@@ -32,11 +32,27 @@ def _model():
     return m.eval()
 
 
-@pytest.mark.parametrize("verify,min_keep", [(False, 1), (True, 1), (False, 2)])
-def test_generate_replays_through_oracle(verify, min_keep):
+def _run(model, verify, min_keep, kw, record=None):
     from flash_dllm_b200.generate import generate_with_Flash_dLLM
     from flash_dllm_b200._lib import check_device_status
+    prompts = cases.gen_prompts()
+    n = len(prompts)
+    resp, steps = [None] * n, [0] * n
+    trace = []
+    resp, ntok, nmax = generate_with_Flash_dLLM(
+        model, [p.cuda() for p in prompts], list(cases.GEN_PROMPT_LENS), cases.GEN_BATCH, resp, steps,
+        gen_length=cases.GEN_LEN[verify], verify=verify, min_keep=min_keep, record=record, trace=trace, **kw)
+    check_device_status()
+    return resp, steps, ntok, nmax, trace
+
+
+@pytest.mark.parametrize("verify,min_keep,track_num", [(False, 1, 1), (True, 1, 1), (False, 2, 1), (False, 1, 2),
+                                                       (True, 1, 2)])
+def test_generate_replays_through_oracle(verify, min_keep, track_num):
+    """track_num 2 is BASELINE config 5's refresh budget (2 blocks of decoded
+    slots refreshed per step)."""
     model = _model()
+    kw = dict(cases.GEN_KW, track_num=track_num)
     recs = []
 
     def record(v, xq, qpos, kpos, logits, rows, scores):
@@ -46,13 +62,7 @@ def test_generate_replays_through_oracle(verify, min_keep):
 
     prompts = cases.gen_prompts()
     n = len(prompts)
-    resp, steps = [None] * n, [0] * n
-    trace = []
-    resp, ntok, nmax = generate_with_Flash_dLLM(
-        model, [p.cuda() for p in prompts], list(cases.GEN_PROMPT_LENS), cases.GEN_BATCH, resp, steps,
-        gen_length=cases.GEN_LEN[verify], verify=verify, min_keep=min_keep, record=record, trace=trace,
-        **cases.GEN_KW)
-    check_device_status()
+    resp, steps, ntok, nmax, trace = _run(model, verify, min_keep, kw, record)
 
     it = iter(recs)
     vocab = cases.GEN_CFG["vocab_size"]
@@ -78,10 +88,33 @@ def test_generate_replays_through_oracle(verify, min_keep):
     o_resp, o_ntok, o_nmax = do.generate(
         replay, [_L() for _ in range(3)], 3, cases.GEN_CFG["d_model"], cases.HEAD_DIM, cases.THETA, torch.float32,
         prompts, list(cases.GEN_PROMPT_LENS), cases.GEN_BATCH, o_resp, o_steps, gen_length=cases.GEN_LEN[verify],
-        verify=verify, min_keep=min_keep, **cases.GEN_KW)
+        verify=verify, min_keep=min_keep, **kw)
     assert next(it, None) is None, "product issued more forwards than the oracle"
     assert steps == o_steps
     assert (ntok, nmax) == (o_ntok, o_nmax)
     assert [list(r) for r in resp] == [[int(t) for t in s.split()] for s in o_resp]
     keeps = [k for t in trace for k in t["keep"].values()]
     assert max(keeps) >= 1 and len(trace) > 3
+
+
+@pytest.mark.parametrize("verify", [False, True])
+def test_generate_is_reproducible(verify):
+    """Two runs of the same prompts give the same trajectory: the attention
+    scores that order the refresh are reduced in a fixed order, so every
+    decision (and every forward's query set) repeats exactly."""
+    model = _model()
+    runs = []
+    for _ in range(2):
+        recs = []
+
+        def record(v, xq, qpos, kpos, logits, rows, scores, recs=recs):
+            recs.append((qpos.cpu(), scores.cpu().clone()))
+
+        runs.append((_run(model, verify, 1, dict(cases.GEN_KW, track_num=2), record), recs))
+    (r0, rec0), (r1, rec1) = runs
+    assert [list(map(int, r)) for r in r0[0]] == [list(map(int, r)) for r in r1[0]]
+    assert r0[1] == r1[1] and r0[2:4] == r1[2:4]
+    assert len(rec0) == len(rec1)
+    for (q0, s0), (q1, s1) in zip(rec0, rec1):
+        assert torch.equal(q0, q1)
+        assert torch.equal(s0, s1)

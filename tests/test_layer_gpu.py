@@ -144,3 +144,47 @@ def test_plain_launches_without_programmatic_dependency():
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "smoke ok" in r.stdout
+
+
+def test_drop_in_matches_the_reference_layer_run():
+    """The operator called with the argument lists the reference's own layer
+    driver was called with (``tests/golden/make_golden.py`` ran the reference
+    ``flash_fused_elastic_cache`` on a reference ``LLaDALlamaBlock``, fp32, in
+    both modes), compared with that run's outputs.  Bars: K/V rows written to
+    the cache 2e-2, accumulated scores 1e-2, block output 4e-2 -- this is bf16
+    against an fp32 run, and the bf16 oracle layer itself sits 1.9e-2 from the
+    fp32 block output after the extra MLP and residual roundings."""
+    import numpy as np
+    from flash_dllm_b200.flash_cache import flash_fused_elastic_cache
+    from flash_dllm_b200.model import LLaDABlockB200, LLaDAConfigB200
+    g = np.load(cases.__file__.replace("cases.py", "layer_fp32.npz"))
+    cfg, w = cases.gen_weights()
+    blk = LLaDABlockB200(LLaDAConfigB200(d_model=cfg.d_model, n_heads=cfg.n_heads, n_layers=cfg.n_layers,
+                                         mlp_hidden_size=cfg.mlp_hidden_size, vocab_size=cfg.vocab_size), 2,
+                         device="cuda", dtype=torch.bfloat16)
+    pre = "model.transformer.blocks.2."
+    blk.load_state_dict({k[len(pre):]: v.bfloat16() for k, v in w.items() if k.startswith(pre)}, strict=True)
+    dev = torch.device("cuda")
+
+    c = cases.cache_case()
+    blk.k_cache, blk.v_cache = c["k_cache"].bfloat16().to(dev), c["v_cache"].bfloat16().to(dev)
+    scores = torch.zeros(2 * cases.LMAX, device=dev)
+    mb, tb = c["masked_blocks"].to(dev), c["tracked_blocks"].to(dev)
+    positions = [c["pos"].to(dev), torch.tensor([], dtype=torch.int32, device=dev),
+                 [c["sin"].to(dev), c["cos"].to(dev)], [], scores, []]
+    lengths = [[-1, -1], None, mb, tb, torch.cat([mb, tb]), [0, 1], 2, cases.LMAX, cases.BLOCK_M, 128, None, False]
+    y = flash_fused_elastic_cache(blk, c["xn"].bfloat16().to(dev), 2, positions, lengths).squeeze(0)
+    pos = c["pos"].to(dev)
+    assert _rel(blk.k_cache[pos], torch.from_numpy(g["cache_k_rows"])) <= TOL
+    assert _rel(blk.v_cache[pos], torch.from_numpy(g["cache_v_rows"])) <= TOL
+    assert _rel(scores, torch.from_numpy(g["cache_scores"])) <= 1e-2
+    assert _rel(y, torch.from_numpy(g["cache_out"])) <= 4e-2
+
+    v = cases.verify_case()
+    blk.k_cache, blk.v_cache = v["k_cache"].bfloat16().to(dev), v["v_cache"].bfloat16().to(dev)
+    positions = [v["pos"].to(dev), v["pos_k"].to(dev), [v["sin"].to(dev), v["cos"].to(dev)], [],
+                 torch.zeros(2 * cases.LMAX, device=dev), v["attn_mask"].to(dev)]
+    lengths = [[-1, -1], v["blocks"].to(dev), None, torch.tensor([], dtype=torch.int32, device=dev), None, [0, 1], 2,
+               cases.LMAX, cases.BLOCK_M, 128, None, True]
+    y = flash_fused_elastic_cache(blk, v["xn"].bfloat16().to(dev), 2, positions, lengths).squeeze(0)
+    assert _rel(y, torch.from_numpy(g["verify_out"])) <= 4e-2

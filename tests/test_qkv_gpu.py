@@ -43,24 +43,24 @@ def _oracle(x, w, pos, kc, vc, sin, cos, n_heads):
     return q, k2, v2
 
 
-@pytest.mark.parametrize("n_rows,d_model,n_slots,env", [
+@pytest.mark.parametrize("n_rows,d_model,n_slots,plan", [
     (64, 4096, 512, {}),                                     # BASELINE config 1 shape
-    (64, 4096, 512, {"FDLLM_QKV_SPLITS": "3"}),              # the same with split-K
-    (64, 4096, 512, {"FDLLM_QKV_BN": "64", "FDLLM_QKV_SPLITS": "1"}),
+    (64, 4096, 512, {"splits": 3}),                          # the same with split-K
+    (64, 4096, 512, {"bn": 64, "splits": 1}),
     (1, 256, 64, {}),
-    (59, 256, 256, {"FDLLM_QKV_SPLITS": "2"}),
+    (59, 256, 256, {"splits": 2}),
     (129, 256, 512, {}),
-    (300, 512, 1024, {"FDLLM_QKV_BN": "64"}),
+    (300, 512, 1024, {"bn": 64}),
     (512, 4096, 1024, {}),
     (256, 4096, 1024, {}),                                   # CTA-pair stream-K kernel (129-256 rows)
-    (300, 512, 1024, {"FDLLM_QKV_PAIR": "1"}),               # ... forced: a half-empty 256-row block
-    (512, 4096, 1024, {"FDLLM_QKV_PAIR": "1"}),              # ... forced: partial tiles, owner fix-ups
+    (300, 512, 1024, {"pair": 1}),                           # ... forced: a half-empty 256-row block
+    (512, 4096, 1024, {"pair": 1}),                          # ... forced: partial tiles, owner fix-ups
+    (384, 4096, 2176, {}),                                   # BASELINE config 5 cache step (4 seqs x 96 rows)
 ])
-def test_qkv_rope_cache_matches_oracle(n_rows, d_model, n_slots, env, monkeypatch):
+def test_qkv_rope_cache_matches_oracle(n_rows, d_model, n_slots, plan, qkv_plan):
     import flash_dllm_b200.ops as ops
     from flash_dllm_b200._lib import check_device_status
-    for k, v in env.items():
-        monkeypatch.setenv(k, v)
+    qkv_plan(**plan)
     n_heads = d_model // 128
     x, w, pos, kc, vc, sin, cos = _case(n_rows, d_model, n_slots, seed=n_rows + d_model)
     dev = torch.device("cuda")
@@ -79,10 +79,12 @@ def test_qkv_rope_cache_matches_oracle(n_rows, d_model, n_slots, env, monkeypatc
     assert torch.equal(vd.cpu()[untouched], vc[untouched])
 
 
-@pytest.mark.parametrize("n_rows", [64, 200])
-def test_verify_qkv_matches_oracle(n_rows):
+@pytest.mark.parametrize("n_rows,d_model", [(64, 1024), (200, 1024), (512, 4096), (256, 4096), (64, 4096)])
+def test_verify_qkv_matches_oracle(n_rows, d_model):
+    """512 x 4096 is the config-4 verify forward on one GPU (8 sequences x 64
+    rows), 256 the CTA-pair path (config 5), 64 one sequence per GPU."""
     import flash_dllm_b200.ops as ops
-    d_model, n_slots = 1024, 512
+    n_slots = 512
     n_heads = d_model // 128
     x, w, pos, kc, vc, sin, cos = _case(n_rows, d_model, n_slots, seed=7 + n_rows)
     pos = torch.randint(0, n_slots, (n_rows,), generator=torch.Generator().manual_seed(3))  # repeats allowed
@@ -127,12 +129,13 @@ def test_rmsnorm_matches_reference_rounding(rows, dim):
     assert _rel(y, ref) <= 8e-3
 
 
-def test_split_k_workspace_reuse_across_shapes():
+def test_split_k_workspace_reuse_across_shapes(qkv_plan):
     """Split-K calls with different tile counts share one workspace: a call
     with few tiles must not leave partial sums where a later call with more
     tiles keeps its counters (all 96 head tiles of d_model 4096 checked)."""
     import flash_dllm_b200.ops as ops
     from flash_dllm_b200._lib import check_device_status
+    qkv_plan(splits=3)
     dev = torch.device("cuda")
     for n_rows, d_model, n_slots in ((64, 1024, 256), (64, 4096, 512), (200, 1024, 512), (64, 4096, 512)):
         n_heads = d_model // 128

@@ -7,6 +7,9 @@ a fixed array inside the library instead of a caller workspace.  This test
 calls it through the C ABI twice in a row and compares each result with the
 regular entry point's, within the tolerance the other QKV tests use, and
 checks that a request needing more scratch than the array holds is refused.
+The array's counter / flag region is zeroed on entry of every call that uses
+it, so calls of different kinds (split-K counters, CTA-pair handoff flags)
+can follow one another on the same array; a mixed sequence checks that.
 The file is collected last so a stop-at-first-failure run has already run
 every other test; it also passes alone in a fresh process."""
 import ctypes
@@ -45,10 +48,10 @@ def _noalloc(lib, x, w, pos, sin, cos, q, kc, vc, n_heads):
 
 
 @pytest.mark.parametrize("n_rows", [64, 256])  # split-K / CTA-pair stream-K partials: both use the scratch
-def test_noalloc_matches_workspace_entry_point_twice(n_rows, monkeypatch):
+def test_noalloc_matches_workspace_entry_point_twice(n_rows, qkv_plan):
     import flash_dllm_b200.ops as ops
     from flash_dllm_b200._lib import check_device_status, lib
-    monkeypatch.setenv("FDLLM_QKV_SPLITS", "3")  # split-K at 64 rows (BASELINE config 1 shape)
+    qkv_plan(splits=3)  # split-K at 64 rows (BASELINE config 1 shape); 256 rows run the CTA-pair kernel
     d_model, n_slots = 4096, 512
     n_heads = d_model // 128
     x, w, pos, kc0, vc0, sin, cos = _inputs(n_rows, d_model, n_slots, seed=11)
@@ -66,10 +69,32 @@ def test_noalloc_matches_workspace_entry_point_twice(n_rows, monkeypatch):
         assert _rel(vc[pos], v_ref[pos]) <= TOL
 
 
-def test_noalloc_refuses_requests_beyond_its_scratch(monkeypatch):
+def test_noalloc_mixed_calls_share_the_array(qkv_plan):
+    """A 64-row split-K call, a 256-row CTA-pair call and a 64-row call again
+    on the one array, each compared with the workspace entry point."""
+    import flash_dllm_b200.ops as ops
+    from flash_dllm_b200._lib import check_device_status, lib
+    qkv_plan(splits=3)
+    d_model, n_slots = 4096, 512
+    n_heads = d_model // 128
+    for k, n_rows in enumerate((64, 256, 64)):
+        x, w, pos, kc0, vc0, sin, cos = _inputs(n_rows, d_model, n_slots, seed=20 + k)
+        q_ref = torch.empty_like(x)
+        k_ref, v_ref = kc0.clone(), vc0.clone()
+        ops.qkv_rope_cache(x, *w, pos, sin, cos, q_ref, k_ref, v_ref, n_heads)
+        check_device_status()
+        q = torch.empty_like(x)
+        kc, vc = kc0.clone(), vc0.clone()
+        assert _noalloc(lib(), x, w, pos, sin, cos, q, kc, vc, n_heads) == 0
+        check_device_status()
+        assert _rel(q, q_ref) <= TOL, (n_rows, _rel(q, q_ref))
+        assert _rel(kc[pos], k_ref[pos]) <= TOL
+        assert _rel(vc[pos], v_ref[pos]) <= TOL
+
+
+def test_noalloc_refuses_requests_beyond_its_scratch(qkv_plan):
     from flash_dllm_b200._lib import lib
-    monkeypatch.setenv("FDLLM_QKV_PAIR", "0")  # the single-CTA kernel,
-    monkeypatch.setenv("FDLLM_QKV_SPLITS", "4")  # 256 rows x 4 K-splits: ~50 MB of partials > 24 MiB
+    qkv_plan(splits=4, pair=0)  # the single-CTA kernel, 256 rows x 4 K-splits: ~50 MB of partials > 24 MiB
     x, w, pos, kc, vc, sin, cos = _inputs(256, 4096, 512, seed=12)
     q = torch.empty_like(x)
     k_before = kc.clone()
