@@ -65,4 +65,12 @@ inline cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// QKV projection + RoPE + scatter through the stream-K GEMM (gemm_sk.cu) and
+// its workspace size.
+int launch_qkv_sk(const void* xn, const void* wq, const void* wk, const void* wv, const int64_t* pos,
+                  const float* rope_sin, const float* rope_cos, void* q_out, void* k_out, void* v_out, int32_t n_rows,
+                  int32_t d_model, int32_t n_heads, int64_t n_slots, void* workspace, size_t workspace_bytes,
+                  int kv_by_slot, cudaStream_t stream);
+size_t qkv_sk_ws_bytes(int32_t n_rows, int32_t d_model);
+
 }  // namespace fdllm

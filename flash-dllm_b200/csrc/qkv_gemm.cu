@@ -881,13 +881,21 @@ struct QkvPlan {
 // automatic.  The first values come from FDLLM_QKV_BN / FDLLM_QKV_SPLITS /
 // FDLLM_QKV_KSUB / FDLLM_QKV_PAIR, read once per process.
 struct QkvOverride {
-  int bn, splits, ksub, pair;
+  int impl, bn, splits, ksub, pair;
 };
 
 QkvOverride& qkv_override() {
-  static QkvOverride o{env_int("FDLLM_QKV_BN", 0), env_int("FDLLM_QKV_SPLITS", 1), env_int("FDLLM_QKV_KSUB", 0),
-                       env_int("FDLLM_QKV_PAIR", -1)};
+  static QkvOverride o{env_int("FDLLM_QKV_IMPL", -1), env_int("FDLLM_QKV_BN", 0), env_int("FDLLM_QKV_SPLITS", 1),
+                       env_int("FDLLM_QKV_KSUB", 0), env_int("FDLLM_QKV_PAIR", -1)};
   return o;
+}
+
+// Kernel choice: the stream-K GEMM above 128 rows (512 rows: 51.7 vs 57.7
+// us), the whole-tile kernel up to 128 (64 rows: 27.2 vs 30.1 us), unless
+// overridden.
+bool qkv_use_sk(int32_t n_rows) {
+  const int impl = qkv_override().impl;
+  return impl == 0 || (impl < 0 && n_rows > 128);
 }
 
 // Units are spread round-robin over one CTA per SM.  Tiles are 128 columns
@@ -1060,11 +1068,12 @@ int launch_qkv(const void* xn, const void* wq, const void* wk, const void* wv, c
 
 extern "C" {
 
-int fdllm_qkv_set_plan(int32_t bn, int32_t splits, int32_t ksub, int32_t pair) {
-  if ((bn != 0 && bn != 64 && bn != 128) || splits < 0 || (ksub != 0 && ksub != 1 && ksub != 2) || pair < -1 ||
-      pair > 1)
+int fdllm_qkv_set_plan(int32_t impl, int32_t bn, int32_t splits, int32_t ksub, int32_t pair) {
+  if (impl < -1 || impl > 1 || (bn != 0 && bn != 64 && bn != 128) || splits < 0 ||
+      (ksub != 0 && ksub != 1 && ksub != 2) || pair < -1 || pair > 1)
     return FDLLM_ERR_ARG;
   fdllm::QkvOverride& o = fdllm::qkv_override();
+  o.impl = impl;
   o.bn = bn;
   o.splits = splits < 1 ? 1 : splits;
   o.ksub = ksub;
@@ -1074,6 +1083,7 @@ int fdllm_qkv_set_plan(int32_t bn, int32_t splits, int32_t ksub, int32_t pair) {
 
 size_t fdllm_qkv_workspace_bytes(int32_t n_rows, int32_t d_model, int32_t n_heads) {
   if (n_rows <= 0 || n_heads <= 0 || d_model != n_heads * 128) return 256;
+  if (fdllm::qkv_use_sk(n_rows)) return fdllm::qkv_sk_ws_bytes(n_rows, d_model);
   return fdllm::qkv_ws_bytes(fdllm::plan_qkv(n_rows, d_model, n_heads));
 }
 
@@ -1081,6 +1091,9 @@ int fdllm_qkv_rope_cache(const void* xn, const void* wq, const void* wk, const v
                          const float* rope_sin, const float* rope_cos, void* q_out, void* k_cache, void* v_cache,
                          int32_t n_rows, int32_t d_model, int32_t n_heads, int64_t n_slots, void* workspace,
                          size_t workspace_bytes, cudaStream_t stream) {
+  if (fdllm::qkv_use_sk(n_rows))
+    return fdllm::launch_qkv_sk(xn, wq, wk, wv, pos, rope_sin, rope_cos, q_out, k_cache, v_cache, n_rows, d_model,
+                                n_heads, n_slots, workspace, workspace_bytes, 1, stream);
   return fdllm::launch_qkv(xn, wq, wk, wv, pos, rope_sin, rope_cos, q_out, k_cache, v_cache, n_rows, d_model,
                            n_heads, n_slots, workspace, workspace_bytes, 1, stream);
 }
@@ -1089,6 +1102,9 @@ int fdllm_verify_qkv(const void* xn, const void* wq, const void* wk, const void*
                      const float* rope_sin, const float* rope_cos, void* q_out, void* k_out, void* v_out,
                      int32_t n_rows, int32_t d_model, int32_t n_heads, int64_t n_slots, void* workspace,
                      size_t workspace_bytes, cudaStream_t stream) {
+  if (fdllm::qkv_use_sk(n_rows))
+    return fdllm::launch_qkv_sk(xn, wq, wk, wv, pos, rope_sin, rope_cos, q_out, k_out, v_out, n_rows, d_model,
+                                n_heads, n_slots, workspace, workspace_bytes, 0, stream);
   return fdllm::launch_qkv(xn, wq, wk, wv, pos, rope_sin, rope_cos, q_out, k_out, v_out, n_rows, d_model,
                            n_heads, n_slots, workspace, workspace_bytes, 0, stream);
 }
@@ -1148,6 +1164,15 @@ extern "C" int fdllm_qkv_rope_cache_noalloc(const void* xn, const void* wq, cons
   using namespace fdllm;
   if (n_rows < 0 || n_heads <= 0 || d_model != n_heads * 128 || n_slots <= 0) return FDLLM_ERR_ARG;
   if (n_rows == 0) return FDLLM_OK;
+  if (qkv_use_sk(n_rows)) {
+    // stream-K kernel: flags, then one partial accumulator per CTA
+    if (qkv_sk_ws_bytes(n_rows, d_model) > kQkvNoAllocScratchBytes) return FDLLM_ERR_SCRATCH_LIMIT;
+    void* scratch = qkv_noalloc_scratch();
+    if (scratch == nullptr) return FDLLM_ERR_CUDA;
+    if (cudaMemsetAsync(scratch, 0, kQkvCounterBytes, stream) != cudaSuccess) return FDLLM_ERR_CUDA;
+    return launch_qkv_sk(xn, wq, wk, wv, pos, rope_sin, rope_cos, q_out, k_cache, v_cache, n_rows, d_model,
+                         n_heads, n_slots, scratch, kQkvNoAllocScratchBytes, 1, stream);
+  }
   const QkvPlan pl = plan_qkv(n_rows, d_model, n_heads);
   if ((pl.splits > 1 || pl.pair) && qkv_ws_bytes(pl) > kQkvNoAllocScratchBytes) return FDLLM_ERR_SCRATCH_LIMIT;
   void* scratch = qkv_noalloc_scratch();

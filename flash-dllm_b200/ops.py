@@ -59,10 +59,61 @@ class Workspace:
 _lib.on_device_error(Workspace.rezero)
 
 
-def set_qkv_plan(bn: int = 0, splits: int = 0, ksub: int = 0, pair: int = -1) -> None:
-    """Override the QKV kernel's plan (tuning and tests); no arguments
-    restore the automatic plan."""
-    call("fdllm_qkv_set_plan", bn, splits, ksub, pair)
+def set_qkv_plan(impl: int = -1, bn: int = 0, splits: int = 0, ksub: int = 0, pair: int = -1) -> None:
+    """Override the QKV kernel's plan (tuning and tests): impl 0 is the
+    stream-K GEMM, 1 the earlier whole-tile kernels with their bn / splits /
+    ksub / pair knobs, -1 automatic; no arguments restore the automatic
+    plan."""
+    call("fdllm_qkv_set_plan", impl, bn, splits, ksub, pair)
+
+
+def set_gemm_plan(bn: int = 0, ksub: int = 0, grid: int = 0) -> None:
+    """Override the stream-K GEMM's tile width, ring stage depth and grid
+    (tuning and tests); no arguments restore the automatic plan."""
+    call("fdllm_gemm_set_plan", bn, ksub, grid)
+
+
+def linear(a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bf16(a @ w.T (+ residual)) on the stream-K tcgen05 GEMM (fp32 sum,
+    one rounding, as torch.addmm).  ``a`` may be a row-strided view."""
+    if a.dim() != 2 or a.dtype != BF16 or not a.is_cuda or a.stride(1) != 1:
+        raise ValueError("a must be a 2-D CUDA bf16 tensor with unit column stride")
+    _check(w, "w", BF16, 2)
+    n_rows, k = a.shape
+    if w.shape[1] != k:
+        raise ValueError(f"shapes {tuple(a.shape)} x {tuple(w.shape)}^T do not match")
+    n = w.shape[0]
+    if a.stride(0) != k and n_rows > 1:
+        a = a.contiguous()
+    if residual is not None:
+        _check(residual, "residual", BF16, 2)
+        if residual.shape != (n_rows, n):
+            raise ValueError("residual must be [rows, n]")
+    y = torch.empty(n_rows, n, dtype=BF16, device=a.device) if out is None else out
+    nbytes = _lib.lib().fdllm_gemm_workspace_bytes(n_rows, n, k, 0)
+    ws = Workspace.get(a.device, nbytes, "gemm")
+    call("fdllm_gemm_bf16", ptr(a), ptr(w), ptr(y), ptr(residual), n_rows, n, k, y.stride(0),
+         residual.stride(0) if residual is not None else 0, ptr(ws), ws.numel(), _stream())
+    return y
+
+
+def linear_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor) -> torch.Tensor:
+    """bf16(silu(a @ W_gate.T)) * (a @ W_up.T) with ``w_gate_up`` the
+    [gate; up] stacked weight [2H, K]; one stream-K GEMM, gate/up never
+    leave the tensor memory."""
+    _check(a, "a", BF16, 2)
+    _check(w_gate_up, "w_gate_up", BF16, 2)
+    n_rows, k = a.shape
+    if w_gate_up.shape[1] != k or w_gate_up.shape[0] % 2:
+        raise ValueError("w_gate_up must be [2H, K]")
+    h = w_gate_up.shape[0] // 2
+    y = torch.empty(n_rows, h, dtype=BF16, device=a.device)
+    nbytes = _lib.lib().fdllm_gemm_workspace_bytes(n_rows, 2 * h, k, 1)
+    ws = Workspace.get(a.device, nbytes, "gemm")
+    call("fdllm_gemm_swiglu", ptr(a), ptr(w_gate_up), ptr(y), n_rows, h, k, y.stride(0), ptr(ws), ws.numel(),
+         _stream())
+    return y
 
 
 def _check(t: torch.Tensor, name: str, dtype=None, dim=None) -> None:

@@ -71,13 +71,46 @@ int fdllm_add_rmsnorm(const void* x, const void* residual, const void* weight, v
 int fdllm_swiglu(const void* gate, const void* up, void* out, int64_t rows, int32_t cols, int64_t ld_in,
                  cudaStream_t stream);
 
-/* Override the QKV kernel's plan (tuning and tests; not thread-safe against concurrent calls):
- * bn = tile width 64 or 128 columns (0: automatic), splits = K splits (0 or 1: none), ksub = 64-wide
- * K sub-tiles per ring slot 1 or 2 (0: automatic), pair = CTA-pair kernel above 128 rows: 1 on,
- * 0 off, -1 automatic.  The initial values come from the FDLLM_QKV_BN / _SPLITS / _KSUB / _PAIR
- * environment variables, read once.  The workspace query follows the current plan.  No reference
- * counterpart (the reference's tile sizes are Triton constexprs). */
-int fdllm_qkv_set_plan(int32_t bn, int32_t splits, int32_t ksub, int32_t pair);
+/* Override the QKV kernel's plan (tuning and tests; not thread-safe against concurrent calls).
+ * impl -1 = automatic (the stream-K GEMM above 128 rows), 0 = the stream-K GEMM (tile width and ring
+ * from fdllm_gemm_set_plan), 1 = the earlier whole-tile kernels, where bn = tile width 64 or 128 columns (0: automatic), splits = K splits
+ * (0 or 1: none), ksub = 64-wide K sub-tiles per ring slot 1 or 2 (0: automatic), pair = CTA-pair
+ * kernel above 128 rows: 1 on, 0 off, -1 automatic.  The initial values come from the
+ * FDLLM_QKV_IMPL / _BN / _SPLITS / _KSUB / _PAIR environment variables, read once.  The workspace
+ * query follows the current plan.  No reference counterpart (the reference's tile sizes are Triton
+ * constexprs). */
+int fdllm_qkv_set_plan(int32_t impl, int32_t bn, int32_t splits, int32_t ksub, int32_t pair);
+
+/* Override the stream-K GEMM's plan (tuning and tests): bn = UMMA tile width 128 or 256 columns,
+ * ksub = 64-wide K sub-tiles per ring stage 1 or 2, grid = CTAs (at most the SM count); 0 =
+ * automatic.  Initial values from FDLLM_GEMM_BN / _KSUB / _GRID, read once.  No reference
+ * counterpart. */
+int fdllm_gemm_set_plan(int32_t bn, int32_t ksub, int32_t grid);
+
+/* Workspace (bytes) of fdllm_gemm_bf16 (swiglu = 0; n_cols = output columns) or
+ * fdllm_gemm_swiglu (swiglu = 1; n_cols = 2 * hidden): stream-K flags and one fp32 partial
+ * accumulator per CTA.  Zero-filled once before first use; the kernel leaves it ready for the next
+ * call (after a call whose device status reported an error, zero it again). */
+size_t fdllm_gemm_workspace_bytes(int32_t n_rows, int32_t n_cols, int32_t k_dim, int32_t swiglu);
+
+/* out[r, c] = bf16(sum_k a[r, k] * w[c, k] (+ residual[r, c])) for r < n_rows, c < n_cols:
+ * a bf16 [n_rows, k_dim] (row stride k_dim), w bf16 [n_cols, k_dim] (nn.Linear weight, no bias),
+ * out / residual bf16 with row strides ld_out / ld_res elements (residual may be NULL).  The sum
+ * is fp32 and rounded once (as torch.addmm).  n_cols a multiple of 32, k_dim of 64.  Persistent
+ * stream-K tcgen05 GEMM (one CTA per SM).
+ * ref llada/flash_cache_triton.py:618-627, 634-636 (attn_out + residual, ff_out + residual) and
+ * llada/model/modeling_llada.py:1484 (the LM head, no residual). */
+int fdllm_gemm_bf16(const void* a, const void* w, void* out, const void* residual, int32_t n_rows, int32_t n_cols,
+                    int32_t k_dim, int64_t ld_out, int64_t ld_res, void* workspace, size_t workspace_bytes,
+                    cudaStream_t stream);
+
+/* SwiGLU MLP input projection in one GEMM: w_gate_up bf16 [2 * hidden, k_dim] is ff_proj's weight
+ * stacked over up_proj's; out bf16 [n_rows, hidden] (row stride ld_out) =
+ * bf16(bf16(silu(bf16(a W_gate^T))) * bf16(a W_up^T)), silu in fp32 -- the rounding points of
+ * act(ff_proj(x)) * up_proj(x) in bf16.  hidden a multiple of 128, k_dim of 64.  The gate and up
+ * activations stay in TMEM.  ref llada/flash_cache_triton.py:628-633. */
+int fdllm_gemm_swiglu(const void* a, const void* w_gate_up, void* out, int32_t n_rows, int32_t hidden, int32_t k_dim,
+                      int64_t ld_out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* Workspace (bytes) fdllm_qkv_rope_cache / fdllm_verify_qkv need for n_rows query rows. */
 size_t fdllm_qkv_workspace_bytes(int32_t n_rows, int32_t d_model, int32_t n_heads);

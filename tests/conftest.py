@@ -27,8 +27,9 @@ def pytest_collection_modifyitems(config, items):
 
 @pytest.fixture
 def qkv_plan():
-    """Set a QKV plan override for one test (``qkv_plan(splits=3)``); the
-    automatic plan is restored afterwards."""
+    """Set a QKV plan override for one test (``qkv_plan(impl=1, splits=3)``);
+    the automatic plan is restored afterwards."""
     from flash_dllm_b200 import ops
     yield ops.set_qkv_plan
     ops.set_qkv_plan()
+    ops.set_gemm_plan()

@@ -45,22 +45,31 @@ def _oracle(x, w, pos, kc, vc, sin, cos, n_heads):
 
 @pytest.mark.parametrize("n_rows,d_model,n_slots,plan", [
     (64, 4096, 512, {}),                                     # BASELINE config 1 shape
-    (64, 4096, 512, {"splits": 3}),                          # the same with split-K
-    (64, 4096, 512, {"bn": 64, "splits": 1}),
     (1, 256, 64, {}),
-    (59, 256, 256, {"splits": 2}),
     (129, 256, 512, {}),
-    (300, 512, 1024, {"bn": 64}),
     (512, 4096, 1024, {}),
-    (256, 4096, 1024, {}),                                   # CTA-pair stream-K kernel (129-256 rows)
-    (300, 512, 1024, {"pair": 1}),                           # ... forced: a half-empty 256-row block
-    (512, 4096, 1024, {"pair": 1}),                          # ... forced: partial tiles, owner fix-ups
+    (256, 4096, 1024, {}),
     (384, 4096, 2176, {}),                                   # BASELINE config 5 cache step (4 seqs x 96 rows)
+    (64, 4096, 512, {"impl": 0}),                            # the stream-K GEMM at every row count
+    (1, 256, 64, {"impl": 0}),
+    (300, 512, 1024, {"impl": 0, "gemm": {"bn": 256}}),
+    (64, 4096, 512, {"impl": 0, "gemm": {"bn": 256}}),
+    (200, 1024, 512, {"impl": 0, "gemm": {"grid": 3}}),      # long ranges: several pieces, several tiles
+    (64, 4096, 512, {"impl": 1, "splits": 3}),               # the earlier kernels: split-K
+    (64, 4096, 512, {"impl": 1, "bn": 64, "splits": 1}),
+    (59, 256, 256, {"impl": 1, "splits": 2}),
+    (300, 512, 1024, {"impl": 1, "bn": 64}),
+    (256, 4096, 1024, {"impl": 1}),                          # CTA-pair stream-K kernel (129-256 rows)
+    (300, 512, 1024, {"impl": 1, "pair": 1}),                # ... forced: a half-empty 256-row block
+    (512, 4096, 1024, {"impl": 1, "pair": 1}),               # ... forced: partial tiles, owner fix-ups
 ])
 def test_qkv_rope_cache_matches_oracle(n_rows, d_model, n_slots, plan, qkv_plan):
     import flash_dllm_b200.ops as ops
     from flash_dllm_b200._lib import check_device_status
+    plan = dict(plan)
+    gemm = plan.pop("gemm", {})
     qkv_plan(**plan)
+    ops.set_gemm_plan(**gemm)
     n_heads = d_model // 128
     x, w, pos, kc, vc, sin, cos = _case(n_rows, d_model, n_slots, seed=n_rows + d_model)
     dev = torch.device("cuda")
@@ -135,7 +144,7 @@ def test_split_k_workspace_reuse_across_shapes(qkv_plan):
     tiles keeps its counters (all 96 head tiles of d_model 4096 checked)."""
     import flash_dllm_b200.ops as ops
     from flash_dllm_b200._lib import check_device_status
-    qkv_plan(splits=3)
+    qkv_plan(impl=1, splits=3)
     dev = torch.device("cuda")
     for n_rows, d_model, n_slots in ((64, 1024, 256), (64, 4096, 512), (200, 1024, 512), (64, 4096, 512)):
         n_heads = d_model // 128

@@ -47,11 +47,11 @@ def _noalloc(lib, x, w, pos, sin, cos, q, kc, vc, n_heads):
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
 
 
-@pytest.mark.parametrize("n_rows", [64, 256])  # split-K / CTA-pair stream-K partials: both use the scratch
+@pytest.mark.parametrize("n_rows", [64, 256])
 def test_noalloc_matches_workspace_entry_point_twice(n_rows, qkv_plan):
     import flash_dllm_b200.ops as ops
     from flash_dllm_b200._lib import check_device_status, lib
-    qkv_plan(splits=3)  # split-K at 64 rows (BASELINE config 1 shape); 256 rows run the CTA-pair kernel
+    qkv_plan(impl=0)  # the stream-K GEMM: its flags and per-CTA partial sums live in the array
     d_model, n_slots = 4096, 512
     n_heads = d_model // 128
     x, w, pos, kc0, vc0, sin, cos = _inputs(n_rows, d_model, n_slots, seed=11)
@@ -69,12 +69,15 @@ def test_noalloc_matches_workspace_entry_point_twice(n_rows, qkv_plan):
         assert _rel(vc[pos], v_ref[pos]) <= TOL
 
 
-def test_noalloc_mixed_calls_share_the_array(qkv_plan):
-    """A 64-row split-K call, a 256-row CTA-pair call and a 64-row call again
-    on the one array, each compared with the workspace entry point."""
+@pytest.mark.parametrize("impl", [0, 1])
+def test_noalloc_mixed_calls_share_the_array(impl, qkv_plan):
+    """Calls of different kinds on the one array, each compared with the
+    workspace entry point: with the stream-K GEMM 64, 256 and 64 rows; with
+    the earlier kernels a 64-row split-K call, a 256-row CTA-pair call and a
+    64-row call again."""
     import flash_dllm_b200.ops as ops
     from flash_dllm_b200._lib import check_device_status, lib
-    qkv_plan(splits=3)
+    qkv_plan(impl=impl, splits=3 if impl else 0)
     d_model, n_slots = 4096, 512
     n_heads = d_model // 128
     for k, n_rows in enumerate((64, 256, 64)):
@@ -94,7 +97,7 @@ def test_noalloc_mixed_calls_share_the_array(qkv_plan):
 
 def test_noalloc_refuses_requests_beyond_its_scratch(qkv_plan):
     from flash_dllm_b200._lib import lib
-    qkv_plan(splits=4, pair=0)  # the single-CTA kernel, 256 rows x 4 K-splits: ~50 MB of partials > 24 MiB
+    qkv_plan(impl=1, splits=4, pair=0)  # the earlier single-CTA kernel, 256 rows x 4 K-splits: ~50 MB > 24 MiB
     x, w, pos, kc, vc, sin, cos = _inputs(256, 4096, 512, seed=12)
     q = torch.empty_like(x)
     k_before = kc.clone()
