@@ -31,7 +31,7 @@ SIGNATURES = {
     "fdllm_add_rmsnorm": (_int, [_p, _p, _p, _p, _p, _i32, _i32, _f32, _p]),
     "fdllm_swiglu": (_int, [_p, _p, _p, _i64, _i32, _i64, _p]),
     "fdllm_qkv_set_plan": (_int, [_i32, _i32, _i32, _i32, _i32]),
-    "fdllm_gemm_set_plan": (_int, [_i32, _i32, _i32]),
+    "fdllm_gemm_set_plan": (_int, [_i32, _i32, _i32, _i32, _i32]),
     "fdllm_gemm_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
     "fdllm_gemm_bf16": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _i64, _i64, _p, _sz, _p]),
     "fdllm_gemm_swiglu": (_int, [_p, _p, _p, _i32, _i32, _i32, _i64, _p, _sz, _p]),

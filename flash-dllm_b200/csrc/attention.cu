@@ -48,7 +48,6 @@ constexpr int kPlanItem = 8;
 constexpr int kPlanSeq = 3;
 constexpr int kAttnKernelId = 2;
 constexpr int kPlanKernelId = 3;
-constexpr int kScoresKernelId = 6;
 
 // Byte offset of 16-byte chunk `chunk` (0..15, 8 dims each) of key row `row`
 // inside a tile stored as two 64-dim halves with the 128-byte swizzle -- the

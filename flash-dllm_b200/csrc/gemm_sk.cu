@@ -35,11 +35,14 @@
 // the flags for the next call.  Every CTA of the grid is resident at once
 // (grid <= SMs, one CTA per SM), and every wait is bounded.
 //
-// Warp roles (192 threads): warp 0 TMA producer into a ring of KSUB x 64-K
+// Warp roles (384 threads): warp 0 TMA producer into a ring of KSUB x 64-K
 // stages (128-byte swizzle), warp 1 TMEM owner and single-thread MMA issuer
 // (M = 128, N = BN) into one of two TMEM accumulators (segments alternate),
-// warps 2-5 the epilogue (thread = TMEM lane = tile row), which overlaps the
-// next segment's MMAs.
+// warps 4-11 the epilogue, which overlaps the next segment's MMAs: two warps
+// per TMEM lane quarter (thread = tile row), each taking every other group
+// of columns, so two groups' memory traffic is in flight at once.  The
+// producer / MMA warpgroup gives registers up (setmaxnreg 48) to the two
+// epilogue warpgroups (224 each).
 #include "common.cuh"
 #include "internal.h"
 
@@ -47,10 +50,14 @@ namespace fdllm {
 
 constexpr int kGBM = 128;
 constexpr int kGBK = 64;
-constexpr int kGThreads = 192;
+constexpr int kGThreads = 384;     // warpgroup 0: producer, MMA, 2 idle; warpgroups 1-2: epilogue
+constexpr int kGEpiThreads = 256;
+constexpr int kGRegsLow = 48, kGRegsHigh = 224;
+static_assert(128 * kGRegsLow + 256 * kGRegsHigh <= kGThreads * 168, "setmaxnreg split");
 constexpr int kGemmKernelId = 7;
-constexpr int kGRingBytes = 192 * 1024;
+constexpr int kGRingBytes = 160 * 1024;
 constexpr size_t kGFlagBytes = 4096;  // one int32 flag per CTA (grid <= 1024)
+constexpr int kGStageBytes = 8 * 32 * 64 * 4;  // epilogue staging: 8 warps x 32 rows x 64 fp32
 
 enum GemmEpi { kEpiQkv = 0, kEpiStore = 1, kEpiSwiglu = 2 };
 
@@ -62,10 +69,10 @@ struct GCfg {
   static constexpr int kStageBytes = KSUB * (kASub + kBSub);
   static constexpr int kStages = kGRingBytes / kStageBytes;
   static constexpr int kBarOffset = kStages * kStageBytes;
-  static constexpr int kSmem = 1024 + kBarOffset + 256;
+  static constexpr int kSmem = 1024 + kBarOffset + kGStageBytes + 256;
   static constexpr int kTmemCols = 2 * BN;
   static_assert(kStages >= 2, "ring depth");
-  static_assert(kSmem <= 227 * 1024, "shared memory");
+  static_assert(kSmem <= 232448, "shared memory");
 };
 
 struct GemmParams {
@@ -113,39 +120,317 @@ __device__ __forceinline__ bool g_next(int& i, int hi, int kbt, GSeg& s) {
   return true;
 }
 
-// 32 accumulator columns [col, col + 32) of this thread's row, plus the
-// partial sums of contributor CTAs [q0, q1) in CTA order.
+// Two 32-column chunks (ca, cb) with their partial sums: both TMEM loads and
+// all partial loads are in flight together (one L2 latency per pair).
+// Contributors [q0, q0 + n_smem) were copied (in order) into shared memory
+// at `spart`; the others are read from the workspace.
 template <int BN>
-__device__ __forceinline__ void g_chunk(uint32_t t_row, int col, const GemmParams& p, int q0, int q1, int r_tile,
-                                        float (&v)[32]) {
+__device__ __forceinline__ void g_chunk2(uint32_t t_row, int ca, int cb, const GemmParams& p, int q0, int q1, int qmul,
+                                         int qadd, const float4* spart, int n_smem, int r_tile, float (&va)[32],
+                                         float (&vb)[32]) {
   __syncwarp();
-  tmem_ld_32x32b_x32(t_row + col, v);
+  tmem_ld2_32x32b_x32(t_row + ca, t_row + cb, va, vb);
   for (int q = q0; q < q1; ++q) {
-    const float4* part = reinterpret_cast<const float4*>(p.partials) + static_cast<size_t>(q) * (kGBM * BN / 4);
+    const float4* part =
+        q - q0 < n_smem
+            ? spart + static_cast<size_t>(q - q0) * (kGBM * BN / 4)
+            : reinterpret_cast<const float4*>(p.partials) + static_cast<size_t>(q * qmul + qadd) * (kGBM * BN / 4);
+    float4 xa[8], xb[8];
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      const float4 x = __ldcg(part + ((col + j) >> 2) * kGBM + r_tile);
-      v[j] += x.x;
-      v[j + 1] += x.y;
-      v[j + 2] += x.z;
-      v[j + 3] += x.w;
+    for (int j = 0; j < 8; ++j) {
+      xa[j] = part[((ca >> 2) + j) * kGBM + r_tile];
+      xb[j] = part[((cb >> 2) + j) * kGBM + r_tile];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      va[4 * j] += xa[j].x;
+      va[4 * j + 1] += xa[j].y;
+      va[4 * j + 2] += xa[j].z;
+      va[4 * j + 3] += xa[j].w;
+      vb[4 * j] += xb[j].x;
+      vb[4 * j + 1] += xb[j].y;
+      vb[4 * j + 2] += xb[j].z;
+      vb[4 * j + 3] += xb[j].w;
     }
   }
 }
 
-__device__ __forceinline__ void g_store32(__nv_bfloat16* dst, const float (&v)[32]) {
+// Pull the rows the epilogue of a tile will read into L2 while its MMAs run
+// (the epilogue's own loads are then L2 hits): the QKV row's RoPE tables
+// (1 KB), or its residual row segment.
+template <int BN, int EPI>
+__device__ __forceinline__ void g_prefetch_epilogue(const GemmParams& p, int row, int n_tile, int64_t slot) {
+  if (EPI == kEpiQkv) {
+    if (slot < 0) return;
 #pragma unroll
-  for (int i = 0; i < 32; i += 8) {
-    uint4 u;
-    u.x = pack_bf16x2(v[i], v[i + 1]);
-    u.y = pack_bf16x2(v[i + 2], v[i + 3]);
-    u.z = pack_bf16x2(v[i + 4], v[i + 5]);
-    u.w = pack_bf16x2(v[i + 6], v[i + 7]);
-    *reinterpret_cast<uint4*>(dst + i) = u;
+    for (int l = 0; l < 128; l += 32) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.sin + slot * 128 + l));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.cos + slot * 128 + l));
+    }
+  } else if (EPI == kEpiStore) {
+    if (p.res == nullptr || row >= p.n_rows) return;
+    const __nv_bfloat16* r = p.res + static_cast<int64_t>(row) * p.ld_res + n_tile * BN;
+    const int n = min(BN, p.n_cols - n_tile * BN);
+    for (int c = 0; c < n; c += 64) asm volatile("prefetch.global.L2 [%0];" ::"l"(r + c));
+  }
+}
+
+// This thread's BN accumulator columns as a contributor's partial sums,
+// [col / 4][row][4] fp32, so a warp's stores are 512 contiguous bytes.
+template <int BN>
+__device__ __forceinline__ void g_publish(uint32_t t_row, const GemmParams& p, int slot, int r_tile, int half) {
+  float4* part = reinterpret_cast<float4*>(p.partials) + static_cast<size_t>(slot) * (kGBM * BN / 4);
+#pragma unroll 1
+  for (int c = half * 64; c < BN; c += 128) {
+    float v[32], w[32];
+    __syncwarp();
+    tmem_ld2_32x32b_x32(t_row + c, t_row + c + 32, v, w);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      __stcg(part + ((c + j) >> 2) * kGBM + r_tile, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+      __stcg(part + ((c + 32 + j) >> 2) * kGBM + r_tile, make_float4(w[j], w[j + 1], w[j + 2], w[j + 3]));
+    }
   }
 }
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ uint4 g_pack8(const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  return u;
+}
+
+// Per-warp staging of 32 rows x 64 fp32 columns (8 KB): the thread of row r
+// writes its two 32-column chunks as 16 float4 units, unit u at position
+// (u & 8) | ((u & 7) ^ (r & 7)) of the row (so the 32 rows spread over the
+// banks); the warp then reads it back with several lanes per row, which makes
+// the epilogue's global loads and stores row-contiguous.
+__device__ __forceinline__ void g_stage_put(float4* stage, int lane, const float (&va)[32], const float (&vb)[32]) {
+  float4* row = stage + lane * 16;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    row[u ^ (lane & 7)] = make_float4(va[4 * u], va[4 * u + 1], va[4 * u + 2], va[4 * u + 3]);
+    row[8 | (u ^ (lane & 7))] = make_float4(vb[4 * u], vb[4 * u + 1], vb[4 * u + 2], vb[4 * u + 3]);
+  }
+}
+// 8 consecutive columns (units u, u + 1; u even) of staged row r
+__device__ __forceinline__ void g_stage_get8(const float4* stage, int r, int u, float (&v)[8]) {
+  const float4 x = stage[r * 16 + ((u & 8) | ((u & 7) ^ (r & 7)))];
+  const float4 y = stage[r * 16 + (((u + 1) & 8) | (((u + 1) & 7) ^ (r & 7)))];
+  v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+  v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+}
+
+// Epilogue of one tile on this CTA's 128 accumulator rows (global rows
+// row0 + r), by the 8 epilogue warps (warp quarter w: rows 32 w .. 32 w + 31;
+// `half` 0 / 1 takes the even / odd column groups).  `slot` is the QKV cache
+// slot of this thread's row (-1: not written).
+template <int BN, int EPI>
+__device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_row, float4* stage, int quarter,
+                                                int half, int lane, int row0, int n_tile, int q0, int q1, int qmul,
+                                                int qadd, const float4* spart, int n_smem, int64_t slot) {
+  const int r_tile = quarter * 32 + lane;
+  const int wrow0 = row0 + quarter * 32;  // global row of the warp's staged row 0
+  if (EPI == kEpiQkv) {
+#pragma unroll 1
+    for (int hh = 0; hh < BN / 128; ++hh) {
+      const int n0 = n_tile * BN + hh * 128;
+      const int proj = n0 / p.d_model;
+      const int hcol = n0 - proj * p.d_model;  // first column of the head in its projection
+      __nv_bfloat16* out = proj == 0 ? p.out0 : (proj == 1 ? p.out1 : p.out2);
+      const bool by_slot = proj > 0 && p.kv_by_slot;
+      {
+        const int ch = half;
+        float va[32], vb[32];
+        g_chunk2<BN>(t_row, hh * 128 + ch * 32, hh * 128 + 64 + ch * 32, p, q0, q1, qmul, qadd, spart, n_smem, r_tile,
+                     va, vb);
+        g_stage_put(stage, lane, va, vb);
+        __syncwarp();
+        // 4 lanes per row: lane takes head columns c .. c + 7 (c = ch * 32 +
+        // 8 sub) and their RoPE partners c + 64 ..; two rows per batch, their
+        // table loads in flight together
+        const int sub = lane & 3;
+        const int c = ch * 32 + 8 * sub;
+#pragma unroll 1
+        for (int it = 0; it < 4; it += 2) {
+          int64_t sl[2];
+          float4 tb[2][8];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            sl[u] = __shfl_sync(0xffffffffu, slot, (it + u) * 8 + (lane >> 2));
+            const int64_t sr = sl[u] < 0 ? 0 : sl[u];
+            const float4* sp = reinterpret_cast<const float4*>(p.sin + sr * 128 + c);
+            const float4* cp = reinterpret_cast<const float4*>(p.cos + sr * 128 + c);
+            if (proj < 2) {
+              tb[u][0] = __ldg(sp);
+              tb[u][1] = __ldg(sp + 1);
+              tb[u][2] = __ldg(sp + 16);
+              tb[u][3] = __ldg(sp + 17);
+              tb[u][4] = __ldg(cp);
+              tb[u][5] = __ldg(cp + 1);
+              tb[u][6] = __ldg(cp + 16);
+              tb[u][7] = __ldg(cp + 17);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int rr = (it + u) * 8 + (lane >> 2);
+            float x1[8], x2[8];
+            g_stage_get8(stage, rr, 2 * sub, x1);
+            g_stage_get8(stage, rr, 8 + 2 * sub, x2);
+            if (sl[u] < 0) continue;
+            if (proj < 2) {
+              const float s1[8] = {tb[u][0].x, tb[u][0].y, tb[u][0].z, tb[u][0].w,
+                                   tb[u][1].x, tb[u][1].y, tb[u][1].z, tb[u][1].w};
+              const float s2[8] = {tb[u][2].x, tb[u][2].y, tb[u][2].z, tb[u][2].w,
+                                   tb[u][3].x, tb[u][3].y, tb[u][3].z, tb[u][3].w};
+              const float c1[8] = {tb[u][4].x, tb[u][4].y, tb[u][4].z, tb[u][4].w,
+                                   tb[u][5].x, tb[u][5].y, tb[u][5].z, tb[u][5].w};
+              const float c2[8] = {tb[u][6].x, tb[u][6].y, tb[u][6].z, tb[u][6].w,
+                                   tb[u][7].x, tb[u][7].y, tb[u][7].z, tb[u][7].w};
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                const float a1 = x1[k], a2 = x2[k];
+                x1[k] = a1 * c1[k] - a2 * s1[k];
+                x2[k] = a2 * c2[k] + a1 * s2[k];
+              }
+            }
+            const int64_t orow = by_slot ? sl[u] : static_cast<int64_t>(wrow0 + rr);
+            __nv_bfloat16* dst = out + orow * p.d_model + hcol + c;
+            *reinterpret_cast<uint4*>(dst) = g_pack8(x1);
+            *reinterpret_cast<uint4*>(dst + 64) = g_pack8(x2);
+          }
+        }
+        __syncwarp();
+      }
+    }
+  } else if (EPI == kEpiStore) {
+#pragma unroll 1
+    for (int g = half * 64; g < BN; g += 128) {
+      const int col0 = n_tile * BN + g;
+      if (col0 >= p.n_cols) break;  // uniform
+      float va[32], vb[32];
+      g_chunk2<BN>(t_row, g, g + 32, p, q0, q1, qmul, qadd, spart, n_smem, r_tile, va, vb);
+      g_stage_put(stage, lane, va, vb);
+      __syncwarp();
+      // 8 lanes per row: lane takes columns col0 + 8 sub .. + 7 of rows
+      // 4 it + lane / 8; the residual loads of all 8 rows are in flight
+      // together
+      const int sub = lane & 7;
+      const int col = col0 + 8 * sub;
+      uint4 rv[8];
+      if (p.res != nullptr) {
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int row = wrow0 + it * 4 + (lane >> 3);
+          rv[it] = (row < p.n_rows && col < p.n_cols)
+                       ? __ldg(reinterpret_cast<const uint4*>(p.res + static_cast<int64_t>(row) * p.ld_res + col))
+                       : make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int rr = it * 4 + (lane >> 3);
+        const int row = wrow0 + rr;
+        float v[8];
+        g_stage_get8(stage, rr, 2 * sub, v);
+        if (row >= p.n_rows || col >= p.n_cols) continue;
+        if (p.res != nullptr) {
+          const uint32_t w[4] = {rv[it].x, rv[it].y, rv[it].z, rv[it].w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+            v[2 * k] += f.x;
+            v[2 * k + 1] += f.y;
+          }
+        }
+        *reinterpret_cast<uint4*>(p.out0 + static_cast<int64_t>(row) * p.ld_out + col) = g_pack8(v);
+      }
+      __syncwarp();
+    }
+  } else {
+    // SwiGLU: accumulator columns [0, BN/2) are gate, [BN/2, BN) the matching up
+#pragma unroll 1
+    for (int c0 = half * 32; c0 < BN / 2; c0 += 64) {
+      float gv[32], uv[32];
+      g_chunk2<BN>(t_row, c0, BN / 2 + c0, p, q0, q1, qmul, qadd, spart, n_smem, r_tile, gv, uv);
+      g_stage_put(stage, lane, gv, uv);
+      __syncwarp();
+      const int sub = lane & 3;
+      const int col = n_tile * (BN / 2) + c0 + 8 * sub;
+#pragma unroll 1
+      for (int it = 0; it < 4; ++it) {
+        const int rr = it * 8 + (lane >> 2);
+        const int row = wrow0 + rr;
+        float g8[8], u8[8];
+        g_stage_get8(stage, rr, 2 * sub, g8);
+        g_stage_get8(stage, rr, 8 + 2 * sub, u8);
+        if (row >= p.n_rows) continue;
+        // silu with the fast exp / divide intrinsics: their few-ulp fp32 error
+        // sits far below the bf16 rounding that follows, and the IEEE forms
+        // serialise into ~140 cycles per element here
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float gb = bf16_round(g8[k]);
+          g8[k] = bf16_round(__fdividef(gb, 1.f + __expf(-gb))) * bf16_round(u8[k]);
+        }
+        *reinterpret_cast<uint4*>(p.out0 + static_cast<int64_t>(row) * p.ld_out + col) = g_pack8(g8);
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// Owner fix-up: copy the partial sums of contributors [q0, q0 + n) into the
+// operand ring at `ring` (idle then: a head piece is its CTA's last segment,
+// and every MMA that read the ring has completed) with bulk copies on
+// `bar`, by one thread; the epilogue then reads them from shared memory.
+template <int BN>
+__device__ __forceinline__ void g_fetch_partials(const GemmParams& p, uint8_t* ring, int q0, int n, int qmul, int qadd,
+                                                 uint64_t* bar) {
+  constexpr uint32_t kSlot = kGBM * BN * 4;
+  constexpr uint32_t kPiece = 32 * 1024;
+  mbar_arrive_expect_tx(bar, static_cast<uint32_t>(n) * kSlot);
+  for (int j = 0; j < n; ++j) {
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.partials) + static_cast<size_t>((q0 + j) * qmul + qadd) * kSlot;
+    for (uint32_t off = 0; off < kSlot; off += kPiece) bulk_load(ring + j * kSlot + off, src + off, kPiece, bar);
+  }
+}
+
+// Cache slot of this thread's row for the QKV epilogue (-1: no row / bad slot).
+__device__ __forceinline__ int64_t g_qkv_slot(const GemmParams& p, int row) {
+  if (row >= p.n_rows) return -1;
+  const int64_t s = p.pos[row];
+  if (s < 0 || s >= p.n_slots) {
+    report(p.status, FDLLM_ERR_INDEX, row, kGemmKernelId);
+    return -1;
+  }
+  return s;
+}
+
+// B rows of column tile n_tile for the load of CTA `rank` of a pair (rank 0
+// for a single CTA; `rows` = B rows per CTA): QKV picks the projection's map.
+template <int EPI>
+__device__ __forceinline__ const CUtensorMap* g_b_coord(const GemmParams& p, int n_tile, int tile_cols, int rank,
+                                                       int rows, const CUtensorMap* m0, const CUtensorMap* m1,
+                                                       const CUtensorMap* m2, int& b_row) {
+  if (EPI == kEpiQkv) {
+    const int n0 = n_tile * tile_cols;
+    const int proj = n0 / p.d_model;
+    b_row = n0 - proj * p.d_model + rank * rows;
+    return proj == 0 ? m0 : (proj == 1 ? m1 : m2);
+  }
+  if (EPI == kEpiSwiglu) {
+    b_row = n_tile * (tile_cols / 2) + (rank ? p.hidden : 0);
+    return m0;
+  }
+  b_row = n_tile * tile_cols + rank * rows;
+  return m0;
+}
 
 template <int BN, int XROWS, int KSUB, int EPI>
 __global__ void __launch_bounds__(kGThreads, 1)
@@ -155,11 +440,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
   using C = GCfg<BN, XROWS, KSUB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+  float4* stage_all = reinterpret_cast<float4*>(smem + C::kBarOffset);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset + kGStageBytes);
   uint64_t* empty = full + C::kStages;
   uint64_t* acc_full = empty + C::kStages;  // [2] MMA -> epilogue
   uint64_t* acc_empty = acc_full + 2;       // [2] epilogue (4 warps) -> MMA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* fix_bar = acc_empty + 2;        // owner fix-up: contributors' partials in the ring
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fix_bar + 1);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -179,8 +466,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], 8);  // 8 epilogue warps
     }
+    mbar_init(fix_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -201,6 +489,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
   pdl_wait();
   pdl_launch_dependents();
 
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kGRegsLow));
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer --
     if (lane == 0) {
@@ -211,15 +501,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
       GSeg sg;
       while (ok && g_next(i, hi, p.kbt, sg)) {
         const int m_tile = p.groups > 1 ? group : sg.tile % m_tiles_in, n_tile = sg.tile / m_tiles_in;
-        const CUtensorMap* map_b = &map_b0;
-        int b_row = n_tile * BN;
-        if (EPI == kEpiQkv) {
-          const int proj = b_row / p.d_model;
-          map_b = proj == 0 ? &map_b0 : (proj == 1 ? &map_b1 : &map_b2);
-          b_row -= proj * p.d_model;
-        } else if (EPI == kEpiSwiglu) {
-          b_row = n_tile * (BN / 2);
-        }
+        int b_row = 0;
+        const CUtensorMap* map_b = g_b_coord<EPI>(p, n_tile, BN, 0, BN, &map_b0, &map_b1, &map_b2, b_row);
         for (int kb = sg.k0; kb < sg.k1; ++kb, ++g) {
           const int s = g % C::kStages;
           const uint32_t ph = (g / C::kStages) & 1;
@@ -283,54 +566,40 @@ __global__ void __launch_bounds__(kGThreads, 1)
         ++seg;
       }
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kGRegsHigh));
     // ---------------------------------------------------------- epilogue --
     const int quarter = warp & 3;
+    const int half = (warp - 4) >> 2;
     const int r_tile = quarter * 32 + lane;
-    const int ep_tid = threadIdx.x - 64;
+    const int ep_tid = threadIdx.x - 128;
+    float4* stage = stage_all + (warp - 4) * (32 * 16);
     int seg = 0;
     int i = lo;
     GSeg sg;
     while (g_next(i, hi, p.kbt, sg)) {
       const int acc = seg & 1;
       const int m_tile = p.groups > 1 ? group : sg.tile % m_tiles_in, n_tile = sg.tile / m_tiles_in;
-      const int row = m_tile * kGBM + r_tile;
-      const bool row_ok = row < p.n_rows;
+      const int row0 = m_tile * kGBM;
       const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      // the QKV epilogue's slot and RoPE rows, fetched while the MMAs run
-      int64_t slot = -1;
-      if (EPI == kEpiQkv && sg.k0 == 0 && row_ok) {
-        const int64_t s = p.pos[row];
-        if (s < 0 || s >= p.n_slots) {
-          report(p.status, FDLLM_ERR_INDEX, row, kGemmKernelId);
-        } else {
-          slot = s;
-        }
-      }
+      // the QKV epilogue's slot, fetched while the MMAs run
+      const int64_t slot = (EPI == kEpiQkv && sg.k0 == 0) ? g_qkv_slot(p, row0 + r_tile) : -1;
+      if (sg.k0 == 0 && half == 0) g_prefetch_epilogue<BN, EPI>(p, row0 + r_tile, n_tile, slot);
       // every epilogue thread reaches the named barriers (all waits are
       // bounded), so the decisions below are uniform over the 4 warps
       if (!mbar_wait(&acc_full[acc], (seg >> 1) & 1, p.status, kGemmKernelId)) *abort_flag = 1;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, 256;" ::: "memory");
       if (*abort_flag != 0) break;
       tc_fence_after();
       if (sg.k0 > 0) {
-        // tail piece (this CTA's first segment): publish the partial sums,
-        // [col / 4][row][4] fp32 so a warp's stores are 512 contiguous bytes
-        float4* part = reinterpret_cast<float4*>(p.partials) + static_cast<size_t>(cta) * (kGBM * BN / 4);
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          float v[32];
-          __syncwarp();
-          tmem_ld_32x32b_x32(t_row + c, v);
-#pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            __stcg(part + ((c + j) >> 2) * kGBM + r_tile, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
-        }
+        // tail piece (this CTA's first segment): publish the partial sums
+        g_publish<BN>(t_row, p, cta, r_tile, half);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
         __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         if (ep_tid == 0) st_release_gpu(p.flags + cta, 1);
         ++seg;
         continue;
@@ -345,100 +614,26 @@ __global__ void __launch_bounds__(kGThreads, 1)
         if (ep_tid == 0)
           for (int q = cta + 1; q < q_end && ok; ++q) ok = flag_wait_set(p.flags + q, p.status, kGemmKernelId);
         if (!ok) *abort_flag = 1;
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         if (*abort_flag != 0) break;
       }
-      const int q0 = cta + 1;
-      if (EPI == kEpiQkv) {
-#pragma unroll 1
-        for (int hh = 0; hh < BN / 128; ++hh) {
-          const int n0 = n_tile * BN + hh * 128;
-          const int proj = n0 / p.d_model;
-          const int hcol = n0 - proj * p.d_model;  // first column of the head in its projection
-          __nv_bfloat16* dst = nullptr;
-          if (slot >= 0) {
-            const int64_t orow = (proj > 0 && p.kv_by_slot) ? slot : static_cast<int64_t>(row);
-            dst = (proj == 0 ? p.out0 : (proj == 1 ? p.out1 : p.out2)) + orow * p.d_model + hcol;
-          }
-#pragma unroll 1
-          for (int ch = 0; ch < 2; ++ch) {
-            float a[32], b[32];
-            g_chunk<BN>(t_row, hh * 128 + ch * 32, p, q0, q_end, r_tile, a);
-            g_chunk<BN>(t_row, hh * 128 + 64 + ch * 32, p, q0, q_end, r_tile, b);
-            if (dst == nullptr) continue;
-            if (proj < 2) {
-              const float* srow = p.sin + slot * 128 + ch * 32;
-              const float* crow = p.cos + slot * 128 + ch * 32;
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                const float4 s1 = __ldg(reinterpret_cast<const float4*>(srow + j));
-                const float4 s2 = __ldg(reinterpret_cast<const float4*>(srow + 64 + j));
-                const float4 c1 = __ldg(reinterpret_cast<const float4*>(crow + j));
-                const float4 c2 = __ldg(reinterpret_cast<const float4*>(crow + 64 + j));
-                const float sa[4] = {s1.x, s1.y, s1.z, s1.w}, sb[4] = {s2.x, s2.y, s2.z, s2.w};
-                const float ca[4] = {c1.x, c1.y, c1.z, c1.w}, cb[4] = {c2.x, c2.y, c2.z, c2.w};
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  const float x1 = a[j + k], x2 = b[j + k];
-                  a[j + k] = x1 * ca[k] - x2 * sa[k];
-                  b[j + k] = x2 * cb[k] + x1 * sb[k];
-                }
-              }
-            }
-            g_store32(dst + ch * 32, a);
-            g_store32(dst + 64 + ch * 32, b);
-          }
-        }
-      } else if (EPI == kEpiStore) {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          const int col = n_tile * BN + c;
-          if (col >= p.n_cols) break;  // uniform; n_cols is a multiple of 32
-          float v[32];
-          g_chunk<BN>(t_row, c, p, q0, q_end, r_tile, v);
-          if (!row_ok) continue;
-          if (p.res != nullptr) {
-            const __nv_bfloat16* rrow = p.res + static_cast<int64_t>(row) * p.ld_res + col;
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              const uint4 u = __ldg(reinterpret_cast<const uint4*>(rrow + j));
-              const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
-                v[j + 2 * k] += f.x;
-                v[j + 2 * k + 1] += f.y;
-              }
-            }
-          }
-          g_store32(p.out0 + static_cast<int64_t>(row) * p.ld_out + col, v);
-        }
-      } else {
-        // SwiGLU: UMMA columns [0, BN/2) are gate, [BN/2, BN) the matching up
-#pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
-          float gv[32], uv[32];
-          g_chunk<BN>(t_row, c, p, q0, q_end, r_tile, gv);
-          g_chunk<BN>(t_row, BN / 2 + c, p, q0, q_end, r_tile, uv);
-          if (!row_ok) continue;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float gb = bf16_round(gv[j]);
-            const float s = bf16_round(gb / (1.f + expf(-gb)));
-            gv[j] = s * bf16_round(uv[j]);
-          }
-          g_store32(p.out0 + static_cast<int64_t>(row) * p.ld_out + n_tile * (BN / 2) + c, gv);
-        }
+      int n_smem = 0;
+      if (q_end > cta + 1) {
+        n_smem = min(q_end - cta - 1, C::kBarOffset / (kGBM * BN * 4));
+        if (ep_tid == 0) g_fetch_partials<BN>(p, smem, cta + 1, n_smem, 1, 0, fix_bar);
+        if (!mbar_wait(fix_bar, 0, p.status, kGemmKernelId)) n_smem = 0;  // (recorded; sums then incomplete)
       }
+      g_tile_epilogue<BN, EPI>(p, t_row, stage, quarter, half, lane, row0, n_tile, cta + 1, q_end, 1, 0,
+                               reinterpret_cast<const float4*>(smem), n_smem, slot);
       // every column of this accumulator has been read
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
-      if (q_end > q0) {
+      if (q_end > cta + 1) {
         // every epilogue thread has read the partials: clear their flags
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         if (ep_tid == 0)
-          for (int q = q0; q < q_end; ++q) p.flags[q] = 0;
+          for (int q = cta + 1; q < q_end; ++q) p.flags[q] = 0;
       }
       ++seg;
     }
@@ -451,55 +646,343 @@ __global__ void __launch_bounds__(kGThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant (more than 128 rows): clusters of two CTAs compute
+// 256-row x 256-column tiles with 2-SM UMMAs (cta_group::2, M = 256): CTA r
+// loads rows 128 r .. 128 r + 127 of the tile's A rows and B rows
+// 128 r .. 128 r + 127 of its 256 columns, and holds its 128 output rows x 256
+// columns in its own TMEM.  Each SM then moves 32 KB of operands per 64-K
+// step for 4.2 MFLOP (a single-CTA 128 x 256 tile: 48 KB), within what one
+// SM pulls from L2.  Stream-K as above, over pairs: pair j of every m-tile
+// group has the same range; a contributor pair's CTAs publish their partial
+// sums and flags separately, and each CTA of the owner pair adds those of
+// its rank.  The leader's `full` barrier expects both CTAs' bytes; stage,
+// accumulator and TMEM-free completions go to both CTAs.
+// ---------------------------------------------------------------------------
+template <int KSUB>
+struct G2Cfg {
+  static constexpr int kSub = kGBM * kGBK * 2;      // 128 rows x 64 K (A, or this CTA's half of B)
+  static constexpr int kABytes = KSUB * kSub;
+  static constexpr int kStageBytes = 2 * KSUB * kSub;
+  static constexpr int kStages = kGRingBytes / kStageBytes;
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kSmem = 1024 + kBarOffset + kGStageBytes + 256;
+  static_assert(kSmem <= 232448, "shared memory");
+};
+
+template <int KSUB, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
+    gemm_sk2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b0,
+                    const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_b2,
+                    const GemmParams p) {
+  using C = G2Cfg<KSUB>;
+  constexpr int BN = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float4* stage_all = reinterpret_cast<float4*>(smem + C::kBarOffset);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset + kGStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;  // [2] leader's MMA -> both CTAs' epilogues
+  uint64_t* acc_empty = acc_full + 2;       // [2] both epilogues (8 warps) -> leader's MMA
+  uint64_t* fix_bar = acc_empty + 2;        // owner fix-up: contributors' partials in the ring
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fix_bar + 1);
+  volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cta = blockIdx.x;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = cta >> 1;
+  const int n_pairs = gridDim.x >> 1;
+  const int per_group = n_pairs / p.groups;
+  const int group = pair / per_group;
+  const int idx = pair % per_group;
+  const int lo = g_lo(idx, per_group, p.iters);
+  const int hi = g_lo(idx + 1, per_group, p.iters);
+  const int m_tiles_in = p.groups > 1 ? 1 : p.m_tiles;  // m-tiles of 256 rows
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);   // the leader's expect_tx arrival (used on the leader)
+      mbar_init(&empty[s], 1);  // the leader's commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 16);  // 8 epilogue warps x 2 CTAs (used on the leader)
+    }
+    mbar_init(fix_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b0);
+    if (EPI == kEpiQkv) {
+      tma_prefetch_desc(&map_b1);
+      tma_prefetch_desc(&map_b2);
+    }
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  pdl_launch_dependents();
+
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kGRegsLow));
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer --
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      int i = lo;
+      GSeg sg;
+      while (ok && g_next(i, hi, p.kbt, sg)) {
+        const int m_tile = p.groups > 1 ? group : sg.tile % m_tiles_in, n_tile = sg.tile / m_tiles_in;
+        const int a_row = m_tile * 2 * kGBM + static_cast<int>(rank) * kGBM;
+        int b_row = 0;
+        const CUtensorMap* map_b =
+            g_b_coord<EPI>(p, n_tile, BN, static_cast<int>(rank), kGBM, &map_b0, &map_b1, &map_b2, b_row);
+        for (int kb = sg.k0; kb < sg.k1; ++kb, ++g) {
+          const int s = g % C::kStages;
+          const uint32_t ph = (g / C::kStages) & 1;
+          if (g >= static_cast<uint32_t>(C::kStages) && !mbar_wait(&empty[s], ph ^ 1, p.status, kGemmKernelId)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a0 = smem + s * C::kStageBytes;
+          const uint32_t bar = mapa_shared(&full[s], 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2u * C::kStageBytes);
+#pragma unroll
+          for (int sub = 0; sub < KSUB; ++sub) {
+            const int kx = (kb * KSUB + sub) * kGBK;
+            tma_load_2d_pair(a0 + sub * C::kSub, &map_a, kx, a_row, bar);
+            tma_load_2d_pair(a0 + C::kABytes + sub * C::kSub, map_b, kx, b_row, bar);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------- MMA issuer (leader only) --
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(2 * kGBM, BN);
+      uint32_t g = 0;
+      int seg = 0;
+      bool ok = true;
+      int i = lo;
+      GSeg sg;
+      while (ok && g_next(i, hi, p.kbt, sg)) {
+        const int acc = seg & 1;
+        if (seg >= 2 && !mbar_wait(&acc_empty[acc], ((seg >> 1) & 1) ^ 1, p.status, kGemmKernelId)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = sg.k0; kb < sg.k1; ++kb, ++g) {
+          const int s = g % C::kStages;
+          const uint32_t ph = (g / C::kStages) & 1;
+          if (!mbar_wait(&full[s], ph, p.status, kGemmKernelId)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* a0 = smem + s * C::kStageBytes;
+#pragma unroll
+          for (int sub = 0; sub < KSUB; ++sub) {
+            const uint64_t da = umma_desc_kmajor_sw128(smem_u32(a0 + sub * C::kSub));
+            const uint64_t db = umma_desc_kmajor_sw128(smem_u32(a0 + C::kABytes + sub * C::kSub));
+#pragma unroll
+            for (int k = 0; k < kGBK / 16; ++k)
+              umma_bf16_pair(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb > sg.k0 || sub > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(mapa_shared(&empty[s], 0));
+          umma_commit_pair(mapa_shared(&empty[s], 1));
+        }
+        if (!ok) break;
+        umma_commit_pair(mapa_shared(&acc_full[acc], 0));
+        umma_commit_pair(mapa_shared(&acc_full[acc], 1));
+        ++seg;
+      }
+    }
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kGRegsHigh));
+    // ---------------------------------------------------------- epilogue --
+    const int quarter = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const int r_tile = quarter * 32 + lane;
+    const int ep_tid = threadIdx.x - 128;
+    float4* stage = stage_all + (warp - 4) * (32 * 16);
+    const uint32_t acc_empty_leader[2] = {mapa_shared(&acc_empty[0], 0), mapa_shared(&acc_empty[1], 0)};
+    int seg = 0;
+    int i = lo;
+    GSeg sg;
+    while (g_next(i, hi, p.kbt, sg)) {
+      const int acc = seg & 1;
+      const int m_tile = p.groups > 1 ? group : sg.tile % m_tiles_in, n_tile = sg.tile / m_tiles_in;
+      const int row0 = m_tile * 2 * kGBM + static_cast<int>(rank) * kGBM;
+      const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+      const int64_t slot = (EPI == kEpiQkv && sg.k0 == 0) ? g_qkv_slot(p, row0 + r_tile) : -1;
+      if (sg.k0 == 0 && half == 0) g_prefetch_epilogue<BN, EPI>(p, row0 + r_tile, n_tile, slot);
+      if (!mbar_wait(&acc_full[acc], (seg >> 1) & 1, p.status, kGemmKernelId)) *abort_flag = 1;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (*abort_flag != 0) break;
+      tc_fence_after();
+      if (sg.k0 > 0) {
+        g_publish<BN>(t_row, p, cta, r_tile, half);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc_empty_leader[acc]);
+        __threadfence();
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (ep_tid == 0) st_release_gpu(p.flags + cta, 1);
+        ++seg;
+        continue;
+      }
+      int q_end = pair + 1;  // contributor pairs: the next pairs of the group
+      if (sg.k1 < p.kbt) {
+        const int t_end = (sg.tile + 1) * p.kbt;
+        while (q_end - group * per_group < per_group && g_lo(q_end - group * per_group, per_group, p.iters) < t_end)
+          ++q_end;
+        bool ok = true;
+        if (ep_tid == 0)
+          for (int q = pair + 1; q < q_end && ok; ++q)
+            ok = flag_wait_set(p.flags + 2 * q + static_cast<int>(rank), p.status, kGemmKernelId);
+        if (!ok) *abort_flag = 1;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (*abort_flag != 0) break;
+      }
+      int n_smem = 0;
+      if (q_end > pair + 1) {
+        n_smem = min(q_end - pair - 1, C::kBarOffset / (kGBM * BN * 4));
+        if (ep_tid == 0) g_fetch_partials<BN>(p, smem, pair + 1, n_smem, 2, static_cast<int>(rank), fix_bar);
+        if (!mbar_wait(fix_bar, 0, p.status, kGemmKernelId)) n_smem = 0;  // (recorded; sums then incomplete)
+      }
+      g_tile_epilogue<BN, EPI>(p, t_row, stage, quarter, half, lane, row0, n_tile, pair + 1, q_end, 2,
+                               static_cast<int>(rank), reinterpret_cast<const float4*>(smem), n_smem, slot);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_leader[acc]);
+      if (q_end > pair + 1) {
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (ep_tid == 0)
+          for (int q = pair + 1; q < q_end; ++q) p.flags[2 * q + static_cast<int>(rank)] = 0;
+      }
+      ++seg;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the leader's MMAs read both CTAs' shared memory until here
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * BN);
+  }
+}
+
 namespace {
 
 struct GemmPlan {
+  bool pair;  // CTA-pair kernel (256-row tiles)
   int bn, xrows, ksub, grid, groups;
   int m_tiles, n_tiles, kbt, iters;
 };
 
-// Plan overrides for tuning and tests (fdllm_gemm_set_plan): 0 = automatic.
+// Plan overrides for tuning and tests (fdllm_gemm_set_plan): 0 / -1 = automatic.
 struct GemmOverride {
-  int bn, ksub, grid;
+  int bn, ksub, grid, pair, dp;
 };
 GemmOverride& gemm_override() {
-  static GemmOverride o{env_int("FDLLM_GEMM_BN", 0), env_int("FDLLM_GEMM_KSUB", 0), env_int("FDLLM_GEMM_GRID", 0)};
+  static GemmOverride o{env_int("FDLLM_GEMM_BN", 0), env_int("FDLLM_GEMM_KSUB", 0), env_int("FDLLM_GEMM_GRID", 0),
+                        env_int("FDLLM_GEMM_PAIR", -1), env_int("FDLLM_GEMM_DP", 0)};
   return o;
 }
 
-// Tile width: 128 columns up to 128 rows (the kernel streams weights from
-// HBM; narrower tiles give more tiles, so fewer stream-K pieces per tile),
-// 256 above (the kernel is bound by operand ingress per SM: a 128 x 256 tile
-// moves 48 KB per 64-K step for 4.2 MFLOP, a 128 x 128 one 32 KB for 2.1).
+// Resident 2-CTA clusters of a pair-kernel configuration (an SM count that
+// is odd within a GPC leaves SMs out); cached per device and configuration.
+template <int KSUB, int EPI>
+int g2_max_pairs() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (cache[dev] == 0) {
+    using C = G2Cfg<KSUB>;
+    if (cudaFuncSetAttribute(gemm_sk2_kernel<KSUB, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+        cudaSuccess)
+      return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(kGThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_sk2_kernel<KSUB, EPI>, &cfg) != cudaSuccess || n <= 0) return 0;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+int g2_max_pairs_for(int epi, int ksub) {
+  if (epi == kEpiQkv) return ksub == 2 ? g2_max_pairs<2, kEpiQkv>() : g2_max_pairs<1, kEpiQkv>();
+  if (epi == kEpiStore) return ksub == 2 ? g2_max_pairs<2, kEpiStore>() : g2_max_pairs<1, kEpiStore>();
+  return ksub == 2 ? g2_max_pairs<2, kEpiSwiglu>() : g2_max_pairs<1, kEpiSwiglu>();
+}
+
+// Up to 128 rows: single CTAs with 128-column tiles, stream-K (the kernel
+// streams weights from HBM; narrower tiles give more tiles, so fewer
+// stream-K pieces per tile).  Above: CTA pairs with 256 x 256 tiles, stream-K
+// (bound by operand ingress per SM, which a pair halves for B) -- except
+// short-K problems whose 128 x 128 tiles all fit the grid at once (attn_out:
+// 4096 x 4096 at up to 4 x 128 rows), which run one whole tile per CTA with
+// no fix-ups.  Ring stages: two 64-K boxes (256 B of every operand row per
+// request) for 64-row single CTAs, one 64-K box elsewhere.
 GemmPlan plan_gemm(int epi, int32_t n_rows, int32_t n_cols, int32_t k_dim, int32_t d_model) {
   GemmPlan pl{};
   const GemmOverride& ov = gemm_override();
-  pl.xrows = n_rows <= 64 ? 64 : 128;
-  int bn = ov.bn == 128 || ov.bn == 256 ? ov.bn : (n_rows <= 128 ? 128 : 256);
-  if (epi == kEpiQkv && d_model % bn != 0) bn = 128;
-  pl.bn = bn;
-  // two 64-K boxes per stage measured faster at every shape (256 B of every
-  // weight row per request): 512 rows 51.7 vs 68.6 us (BN 256), 64 rows
-  // 30.2 vs 31.1 us (BN 128)
-  int ksub = ov.ksub == 1 || ov.ksub == 2 ? ov.ksub : 2;
+  const int out_cols = epi == kEpiSwiglu ? n_cols / 2 : n_cols;
+  bool dp = ov.dp > 0;
+  if (ov.pair < 0 && ov.dp == 0 && n_rows > kGBM && k_dim <= 4096) {
+    const long long tiles128 = static_cast<long long>((n_rows + kGBM - 1) / kGBM) *
+                               ((out_cols + (epi == kEpiSwiglu ? 63 : 127)) / (epi == kEpiSwiglu ? 64 : 128));
+    if (tiles128 <= sm_count()) dp = true;
+  }
+  pl.pair = ov.pair < 0 ? (n_rows > kGBM && !dp) : ov.pair != 0;
+  if (epi == kEpiQkv && d_model % 256 != 0) pl.pair = false;  // a pair tile holds two heads of one projection
+  int bn;
+  if (pl.pair) {
+    bn = 256;
+    pl.xrows = kGBM;
+    pl.m_tiles = (n_rows + 2 * kGBM - 1) / (2 * kGBM);
+  } else {
+    bn = ov.bn == 128 || ov.bn == 256 ? ov.bn : 128;
+    if (epi == kEpiQkv && d_model % bn != 0) bn = 128;
+    pl.xrows = n_rows <= 64 ? 64 : kGBM;
+    pl.m_tiles = (n_rows + kGBM - 1) / kGBM;
+  }
+  int ksub = ov.ksub == 1 || ov.ksub == 2 ? ov.ksub : (!pl.pair && pl.xrows == 64 ? 2 : 1);
+  if (!pl.pair && bn == 256 && pl.xrows == kGBM) ksub = 1;  // a 96 KB stage leaves one stage
   if (k_dim % (kGBK * ksub) != 0) ksub = 1;
   pl.ksub = ksub;
-  pl.m_tiles = (n_rows + kGBM - 1) / kGBM;
-  const int out_per_tile = epi == kEpiSwiglu ? bn / 2 : bn;
-  const int out_cols = epi == kEpiSwiglu ? n_cols / 2 : n_cols;
-  pl.n_tiles = (out_cols + out_per_tile - 1) / out_per_tile;
   pl.kbt = k_dim / (kGBK * ksub);
-  // every CTA must be resident at once (owners wait for contributors), so
-  // the grid never exceeds the SM count (one CTA per SM)
-  int grid = sm_count();
-  if (ov.grid > 0 && ov.grid < grid) grid = ov.grid;
-  if (grid > 1024) grid = 1024;
-  pl.groups = pl.m_tiles <= grid ? pl.m_tiles : 1;
+  pl.bn = bn;
+  const int out_per_tile = epi == kEpiSwiglu ? bn / 2 : bn;
+  pl.n_tiles = (out_cols + out_per_tile - 1) / out_per_tile;
+  // every CTA must be resident at once (owners wait for contributors): at
+  // most one CTA per SM, or the resident pairs
+  int units = pl.pair ? g2_max_pairs_for(epi, ksub) : sm_count();
+  if (units <= 0) units = pl.pair ? sm_count() / 2 : sm_count();
+  if (ov.grid > 0 && ov.grid < units) units = ov.grid;
+  if (units > (pl.pair ? 512 : 1024)) units = pl.pair ? 512 : 1024;
+  pl.groups = pl.m_tiles <= units ? pl.m_tiles : 1;
   const long long iters = static_cast<long long>(pl.groups > 1 ? 1 : pl.m_tiles) * pl.n_tiles * pl.kbt;
   pl.iters = iters > (1ll << 30) ? -1 : static_cast<int>(iters);
-  int per_group = grid / pl.groups;
+  int per_group = units / pl.groups;
   if (pl.iters > 0 && per_group > pl.iters) per_group = pl.iters;
-  pl.grid = per_group * pl.groups;
+  // data-parallel: at most one whole tile per CTA (no fix-ups) when the
+  // tiles fit the grid
+  const int tiles_per_group = pl.groups > 1 ? pl.n_tiles : pl.m_tiles * pl.n_tiles;
+  if (dp && tiles_per_group <= per_group) per_group = tiles_per_group;
+  pl.grid = per_group * pl.groups * (pl.pair ? 2 : 1);
   return pl;
 }
 
@@ -526,9 +1009,24 @@ int launch_gemm_cfg(const CUtensorMap& ma, const CUtensorMap& mb0, const CUtenso
   return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
 }
 
+template <int KSUB, int EPI>
+int launch_gemm2_cfg(const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1, const CUtensorMap& mb2,
+                     const GemmParams& p, int grid, cudaStream_t stream) {
+  using C = G2Cfg<KSUB>;
+  if (g2_max_pairs<KSUB, EPI>() <= 0) return FDLLM_ERR_CUDA;  // also sets the shared-memory attribute
+  // the kernel's __cluster_dims__ gives the pairs; no cluster attribute here
+  if (launch_ex(gemm_sk2_kernel<KSUB, EPI>, dim3(grid), dim3(kGThreads), C::kSmem, stream, 1, pdl_enabled(), ma, mb0,
+                mb1, mb2, p) != cudaSuccess)
+    return FDLLM_ERR_CUDA;
+  return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
+}
+
 template <int EPI>
 int dispatch_gemm(const GemmPlan& pl, const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1,
                   const CUtensorMap& mb2, const GemmParams& p, cudaStream_t stream) {
+  if (pl.pair)
+    return pl.ksub == 2 ? launch_gemm2_cfg<2, EPI>(ma, mb0, mb1, mb2, p, pl.grid, stream)
+                        : launch_gemm2_cfg<1, EPI>(ma, mb0, mb1, mb2, p, pl.grid, stream);
   if (pl.bn == 256) {
     if (pl.xrows == 64)
       return pl.ksub == 2 ? launch_gemm_cfg<256, 64, 2, EPI>(ma, mb0, mb1, mb2, p, pl.grid, stream)
@@ -547,7 +1045,7 @@ int run_gemm(int epi, const void* a, int64_t lda, const void* const* w, int n_w,
              int32_t n_cols, int32_t k_dim, GemmParams& p, void* workspace, size_t workspace_bytes,
              cudaStream_t stream) {
   const GemmPlan pl = plan_gemm(epi, n_rows, n_cols, k_dim, p.d_model);
-  if (pl.iters <= 0) return FDLLM_ERR_ARG;
+  if (pl.iters <= 0 || pl.grid <= 0) return FDLLM_ERR_ARG;
   if (workspace == nullptr || workspace_bytes < gemm_ws_bytes(pl) || !aligned16(workspace))
     return FDLLM_ERR_WORKSPACE;
   p.groups = pl.groups;
@@ -564,7 +1062,8 @@ int run_gemm(int epi, const void* a, int64_t lda, const void* const* w, int n_w,
   CUtensorMap ma, mb[3];
   int rc;
   if ((rc = make_tmap_bf16_sw128(&ma, a, n_rows, k_dim, lda, pl.xrows)) != FDLLM_OK) return rc;
-  const uint32_t box = epi == kEpiSwiglu ? pl.bn / 2 : pl.bn;
+  // B box: the rows one CTA loads per operand box
+  const uint32_t box = pl.pair ? kGBM : (epi == kEpiSwiglu ? pl.bn / 2 : pl.bn);
   for (int i = 0; i < n_w; ++i)
     if ((rc = make_tmap_bf16_sw128(&mb[i], w[i], w_rows, k_dim, k_dim, box)) != FDLLM_OK) return rc;
   for (int i = n_w; i < 3; ++i) mb[i] = mb[0];
@@ -609,13 +1108,16 @@ size_t qkv_sk_ws_bytes(int32_t n_rows, int32_t d_model) {
 
 extern "C" {
 
-int fdllm_gemm_set_plan(int32_t bn, int32_t ksub, int32_t grid) {
-  if ((bn != 0 && bn != 128 && bn != 256) || (ksub != 0 && ksub != 1 && ksub != 2) || grid < 0 || grid > 1024)
+int fdllm_gemm_set_plan(int32_t bn, int32_t ksub, int32_t grid, int32_t pair, int32_t dp) {
+  if ((bn != 0 && bn != 128 && bn != 256) || (ksub != 0 && ksub != 1 && ksub != 2) || grid < 0 || grid > 1024 ||
+      pair < -1 || pair > 1 || dp < 0 || dp > 1)
     return FDLLM_ERR_ARG;
   fdllm::GemmOverride& o = fdllm::gemm_override();
   o.bn = bn;
   o.ksub = ksub;
   o.grid = grid;
+  o.pair = pair;
+  o.dp = dp;
   return FDLLM_OK;
 }
 

@@ -14,19 +14,53 @@ The attention half runs on this package's sm_100a kernels: RMSNorm, the
 tcgen05 QKV + RoPE + cache-scatter GEMM (or its verify variant), and one
 fused masked + tracked attention pass (or the verify attention).  The
 reference's ``S`` tensor and ``attn_scores += S.mean((0, 1))`` become an
-in-kernel accumulation.  After attention, the projections (``attn_out``,
-``ff_proj``/``up_proj`` -- one GEMM when the model stacked their weights as
-``ffup_weight`` -- and ``ff_out``) are the block's own weights through
-cuBLAS, as in the reference, with both residual adds in the GEMM epilogues
-(``addmm``) and SiLU times the gate in one kernel.
+in-kernel accumulation.  After attention the projections run on the
+package's stream-K tcgen05 GEMM with fused epilogues: ``attn_out`` with the
+residual add, ``ff_proj``/``up_proj`` as one GEMM over the stacked
+``ffup_weight`` whose epilogue forms bf16(silu(gate)) * up (the gate and up
+activations never reach HBM), and ``ff_out`` with the residual add.
+Each projection runs on the GEMM that measured faster at its row count
+(``use_own``): this package's for the stacked MLP projection at every row
+count and for ``attn_out`` up to 128 rows; cuBLAS (``addmm``, residual in
+its epilogue too) for ``ff_out`` and for ``attn_out`` above 128 rows.  The
+environment variable ``FDLLM_OWN_GEMMS`` (a comma list of ``attn_out``,
+``mlp``, ``ff_out``, ``lm_head``, ``all`` or ``none``) forces the choice for
+comparisons (``lm_head``: the model's LM head, in ``model.py``).
 """
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
 from . import ops
+
+
+def _own_gemms():
+    v = os.environ.get("FDLLM_OWN_GEMMS")
+    names = ("attn_out", "mlp", "ff_out", "lm_head")
+    if v is None:
+        return None
+    on = {x.strip() for x in v.split(",")}
+    return {n: (n in on or "all" in on) for n in names}
+
+
+OWN_GEMMS = _own_gemms()
+
+# Rows up to which this package's GEMM measured faster than cuBLAS, per
+# projection (B200, LLaDA-8B shapes, back-to-back launches over weights
+# larger than L2): attn_out 19.0 vs 25.4 us at 64 rows, 25.3 vs 21.0 at 512;
+# the stacked MLP with SwiGLU 47.5 vs 43.1 + 8.2 us (cuBLAS + SwiGLU kernel)
+# at 64 rows, 88.3 vs 77.1 + 10.3 at 512; ff_out 32.1 vs 29.3 at 64.
+_OWN_UP_TO = {"attn_out": 128, "mlp": 1 << 30, "ff_out": 0, "lm_head": 0}
+
+
+def use_own(op: str, rows: int) -> bool:
+    """This package's GEMM (True) or cuBLAS (False) for projection `op`."""
+    if OWN_GEMMS is not None:
+        return OWN_GEMMS[op]
+    return rows <= _OWN_UP_TO[op]
 
 
 def _norm_weight(module) -> torch.Tensor:
@@ -108,23 +142,29 @@ def flash_fused_elastic_cache(self, x: torch.Tensor, block_idx, positions, lengt
     plain = _plain_linear(self.attn_out) and _plain_linear(self.ff_out) and isinstance(
         self.dropout, torch.nn.Identity)
     if plain:
-        og_x = torch.addmm(x, att, self.attn_out.weight.t())
+        if use_own("attn_out", n_rows):
+            og_x = ops.linear(att, self.attn_out.weight, residual=x)
+        else:
+            og_x = torch.addmm(x, att, self.attn_out.weight.t())
         h = ops.rmsnorm(og_x, _norm_weight(self.ff_norm), _eps(self.ff_norm))
     else:
         og_x, h = ops.add_rmsnorm(x, self.dropout(self.attn_out(att)), _norm_weight(self.ff_norm),
                                   _eps(self.ff_norm))
     fused = getattr(self, "ffup_weight", None)
-    if fused is not None:  # [ff_proj; up_proj] stacked: one GEMM
-        gu = torch.nn.functional.linear(h, fused)
-        hid = gu.shape[1] // 2
-        gate, up = gu[:, :hid], gu[:, hid:]
+    silu = isinstance(self.act, torch.nn.SiLU)
+    if fused is not None and silu and use_own("mlp", n_rows):
+        h = ops.linear_swiglu(h, fused)  # [ff_proj; up_proj] stacked: one GEMM, SwiGLU in its epilogue
     else:
-        gate, up = self.ff_proj(h), self.up_proj(h)
-    if isinstance(self.act, torch.nn.SiLU):
-        h = ops.swiglu(gate, up)
-    else:
-        h = self.act(gate) * up
+        if fused is not None:
+            gu = torch.nn.functional.linear(h, fused)
+            hid = gu.shape[1] // 2
+            gate, up = gu[:, :hid], gu[:, hid:]
+        else:
+            gate, up = self.ff_proj(h), self.up_proj(h)
+        h = ops.swiglu(gate, up) if silu else self.act(gate) * up
     if plain:
+        if use_own("ff_out", n_rows):
+            return ops.linear(h, self.ff_out.weight, residual=og_x).unsqueeze(0)
         return torch.addmm(og_x, h, self.ff_out.weight.t()).unsqueeze(0)
     h = self.dropout(self.ff_out(h))
     return (og_x + h).unsqueeze(0)

@@ -67,10 +67,11 @@ def set_qkv_plan(impl: int = -1, bn: int = 0, splits: int = 0, ksub: int = 0, pa
     call("fdllm_qkv_set_plan", impl, bn, splits, ksub, pair)
 
 
-def set_gemm_plan(bn: int = 0, ksub: int = 0, grid: int = 0) -> None:
-    """Override the stream-K GEMM's tile width, ring stage depth and grid
-    (tuning and tests); no arguments restore the automatic plan."""
-    call("fdllm_gemm_set_plan", bn, ksub, grid)
+def set_gemm_plan(bn: int = 0, ksub: int = 0, grid: int = 0, pair: int = -1, dp: int = 0) -> None:
+    """Override the stream-K GEMM's tile width, ring stage depth, grid,
+    CTA-pair mode and whole-tile (data-parallel) mode (tuning and tests);
+    no arguments restore the automatic plan."""
+    call("fdllm_gemm_set_plan", bn, ksub, grid, pair, dp)
 
 
 def linear(a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,

@@ -81,11 +81,13 @@ int fdllm_swiglu(const void* gate, const void* up, void* out, int64_t rows, int3
  * constexprs). */
 int fdllm_qkv_set_plan(int32_t impl, int32_t bn, int32_t splits, int32_t ksub, int32_t pair);
 
-/* Override the stream-K GEMM's plan (tuning and tests): bn = UMMA tile width 128 or 256 columns,
- * ksub = 64-wide K sub-tiles per ring stage 1 or 2, grid = CTAs (at most the SM count); 0 =
- * automatic.  Initial values from FDLLM_GEMM_BN / _KSUB / _GRID, read once.  No reference
- * counterpart. */
-int fdllm_gemm_set_plan(int32_t bn, int32_t ksub, int32_t grid);
+/* Override the stream-K GEMM's plan (tuning and tests): bn = single-CTA tile width 128 or 256
+ * columns, ksub = 64-wide K sub-tiles per ring stage 1 or 2, grid = CTAs or CTA pairs (at most
+ * what is resident at once), pair = CTA-pair kernel with 256 x 256 tiles: 1 on, 0 off, dp = 1:
+ * one whole tile per CTA (no stream-K pieces) when the tiles fit the grid; 0 / -1 = automatic
+ * (pairs above 128 rows, stream-K).  Initial values from FDLLM_GEMM_BN / _KSUB / _GRID / _PAIR /
+ * _DP, read once.  No reference counterpart. */
+int fdllm_gemm_set_plan(int32_t bn, int32_t ksub, int32_t grid, int32_t pair, int32_t dp);
 
 /* Workspace (bytes) of fdllm_gemm_bf16 (swiglu = 0; n_cols = output columns) or
  * fdllm_gemm_swiglu (swiglu = 1; n_cols = 2 * hidden): stream-K flags and one fp32 partial

@@ -55,6 +55,6 @@ def test_host_side_queries_and_checks(lib):
                                   None, 0, None) == 1
     assert L.fdllm_qkv_set_plan(1, 96, 1, 0, -1) == 1  # tile width 96 is not a plan
     assert L.fdllm_qkv_set_plan(-1, 0, 0, 0, -1) == 0
-    assert L.fdllm_gemm_set_plan(192, 0, 0) == 1
-    assert L.fdllm_gemm_set_plan(0, 0, 0) == 0
+    assert L.fdllm_gemm_set_plan(192, 0, 0, -1, 0) == 1
+    assert L.fdllm_gemm_set_plan(0, 0, 0, -1, 0) == 0
     assert L.fdllm_gemm_bf16(None, None, None, None, 64, 100, 4096, 100, 0, None, 0, None) == 1  # 100 % 32 != 0

@@ -35,14 +35,19 @@ def _ab(rows, n, k, seed):
     (64, 4096, 4096, {}),               # attn_out, one sequence per GPU
     (64, 4096, 12288, {}),              # ff_out, one sequence per GPU (many pieces per tile)
     (512, 4096, 12288, {}),             # ff_out, eight sequences
-    (512, 4096, 4096, {"bn": 128}),
+    (512, 4096, 4096, {"pair": 0, "bn": 128}),  # single CTAs above 128 rows
+    (256, 2048, 2048, {"ksub": 1}),            # CTA pairs, one 64-K box per stage
+    (64, 1024, 512, {"pair": 1}),              # CTA pairs with the second CTA's rows all outside A
     (300, 1024, 512, {}),               # partial m-tile
     (1, 256, 64, {}),
     (130, 160, 256, {}),                # partial n-tile (160 = 128 + 32 columns)
     (200, 1024, 1024, {"grid": 7}),     # few CTAs: long ranges, pieces of several tiles
     (96, 2048, 2048, {"grid": 1}),      # one CTA: no pieces at all
     (300, 512, 256, {"grid": 2}),       # more m-tiles than CTAs: one group, m-tiles innermost
-    (256, 2048, 2048, {"bn": 256, "ksub": 1}),
+    (512, 4096, 4096, {"pair": 0, "dp": 1}),  # one whole tile per CTA (128 tiles)
+    (512, 4096, 4096, {"dp": 1}),       # CTA pairs, one whole tile each
+    (100, 4096, 1024, {"grid": 30}),    # several contributors per tile, more than fit the ring
+    (256, 2048, 2048, {"pair": 0, "bn": 256, "ksub": 1}),
     (64, 2048, 2048, {"bn": 256, "ksub": 2}),
 ])
 @pytest.mark.parametrize("residual", [False, True])
@@ -82,6 +87,7 @@ def test_gemm_strided_output_and_lm_head_width(gemm_plan):
     (512, 12288, 4096, {}),             # eight sequences
     (37, 512, 256, {"bn": 256}),
     (200, 1024, 512, {"grid": 5}),
+    (200, 1024, 512, {"pair": 0}),
 ])
 def test_gemm_swiglu_matches_torch(rows, h, k, plan, gemm_plan):
     from flash_dllm_b200 import ops

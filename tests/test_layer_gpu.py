@@ -32,9 +32,14 @@ def _blocks(d_model=1024, n_heads=8, hidden=2048):
     return cpu, gpu
 
 
-@pytest.mark.parametrize("fused_mlp", [False, True])
-def test_layer_flash_cache_mode(fused_mlp):
+@pytest.mark.parametrize("fused_mlp,gemms", [(False, None), (True, None), (True, "all"), (True, "none")])
+def test_layer_flash_cache_mode(fused_mlp, gemms, monkeypatch):
+    """`gemms` forces every projection onto this package's GEMM ("all") or
+    cuBLAS ("none"); None is the measured per-shape routing."""
+    import flash_dllm_b200.flash_cache as fc
     from flash_dllm_b200.flash_cache import flash_fused_elastic_cache
+    if gemms is not None:
+        monkeypatch.setattr(fc, "OWN_GEMMS", {n: gemms == "all" for n in ("attn_out", "mlp", "ff_out", "lm_head")})
     d, H, bm, L, B = 1024, 8, 32, 384, 3
     cpu, gpu = _blocks(d, H)
     if fused_mlp:

@@ -52,7 +52,8 @@ def _oracle(x, w, pos, kc, vc, sin, cos, n_heads):
     (384, 4096, 2176, {}),                                   # BASELINE config 5 cache step (4 seqs x 96 rows)
     (64, 4096, 512, {"impl": 0}),                            # the stream-K GEMM at every row count
     (1, 256, 64, {"impl": 0}),
-    (300, 512, 1024, {"impl": 0, "gemm": {"bn": 256}}),
+    (300, 512, 1024, {"impl": 0, "gemm": {"pair": 0, "bn": 256}}),
+    (300, 512, 1024, {"impl": 0, "gemm": {"pair": 1, "ksub": 1}}),
     (64, 4096, 512, {"impl": 0, "gemm": {"bn": 256}}),
     (200, 1024, 512, {"impl": 0, "gemm": {"grid": 3}}),      # long ranges: several pieces, several tiles
     (64, 4096, 512, {"impl": 1, "splits": 3}),               # the earlier kernels: split-K
