@@ -63,8 +63,9 @@ WORKLOADS = {
                     gamma=0.8, track_num=2, verify=True, min_keep=1),
 }
 # DRAM bytes (read + write) of one launch, from an ncu capture of that kernel
-# at that row count (`profiles/`); emitted only for the captured shape.
-NCU_TRAFFIC = {}
+# at that row count (the per-kernel summaries give the commands); emitted
+# only for the captured shape.
+NCU_TRAFFIC = {("mlp", 512): 226365696 + 28009984, ("qkv", 512): 115130112 + 15469568}
 
 
 def _workload(name: str) -> dict:
@@ -465,10 +466,14 @@ def main():
     ap.add_argument("--kernels-only", type=int, default=0, metavar="SEQS",
                     help="time only the hot kernels of one random LLaDA-8B layer at the step shape of SEQS "
                          "sequences per GPU (small case for ncu captures)")
+    ap.add_argument("--only", default="", help="with --kernels-only: launch only this kernel (qkv, attn, "
+                    "verify_attn, mlp, attn_out, ff_out) 4 times")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.kernels_only:
+        if args.only:
+            return run_one_kernel(args.only, args.kernels_only, _workload(args.workload))
         return run_kernels_only(args.kernels_only, _workload(args.workload))
     assert args.warmup >= 3, "at least 3 warm-up steps"
     w = _workload(args.workload)
@@ -614,6 +619,84 @@ def main():
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_one_kernel(name: str, seqs: int, w: dict, reps: int = 4) -> None:
+    """`reps` launches of one hot kernel at the per-GPU step shape of `seqs`
+    sequences (random inputs; a small case for ncu captures): qkv, attn,
+    verify_attn, mlp, attn_out, ff_out (the last three on this package's
+    GEMM whatever the routing)."""
+    from flash_dllm_b200 import ops
+    from flash_dllm_b200._lib import check_device_status
+    from flash_dllm_b200.generate import _verify_mask, get_rotary_embedding
+    dev = torch.device("cuda", 0)
+    d, H, hid = 4096, 32, 12288
+    bm, lmax = w["block_length"], w["seq_len"]
+    per = bm + bm * w["track_num"]
+    n_rows = per * seqs
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rnd(*shape, std=1.0):
+        return (torch.randn(*shape, device=dev, generator=g) * std).to(torch.bfloat16)
+
+    x = rnd(n_rows, d)
+    if name == "qkv":
+        W = [rnd(d, d, std=0.02) for _ in range(3)]
+        pos = torch.stack([torch.randperm(lmax, device=dev, generator=g)[:per] + j * lmax
+                           for j in range(seqs)]).reshape(-1)
+        kc, vc = rnd(seqs * lmax, d), rnd(seqs * lmax, d)
+        sin, cos = get_rotary_embedding(lmax, 128, 500000.0, dev)
+        sin, cos = sin.repeat(seqs, 1).contiguous(), cos.repeat(seqs, 1).contiguous()
+        q = torch.empty_like(x)
+        fn = lambda: ops.qkv_rope_cache(x, W[0], W[1], W[2], pos, sin, cos, q, kc, vc, H)  # noqa: E731
+    elif name in ("attn", "verify_attn"):
+        kc, vc = rnd(seqs * lmax, d), rnd(seqs * lmax, d)
+        o = torch.empty_like(x)
+        if name == "attn":
+            mrows = [(j, lmax, j * bm, (j + 1) * bm) for j in range(seqs)]
+            trows = []
+            for j in range(seqs):
+                s0 = seqs * bm + j * (per - bm)
+                for r0 in range(s0, s0 + per - bm, bm):
+                    trows.append((j, lmax, r0, min(r0 + bm, s0 + per - bm)))
+            mb = torch.tensor(mrows, dtype=torch.int64, device=dev)
+            tb = torch.tensor(trows, dtype=torch.int64, device=dev).reshape(-1, 4)
+            plan, cap = ops.plan_cache_attention(mb, tb, n_rows, seqs, bm, lmax, dev)
+            scores = torch.zeros(seqs * lmax, device=dev)
+            fn = lambda: ops.attn_cache(x, o, kc, vc, plan, cap, scores, 1.0 / (bm * H), H, lmax,  # noqa: E731
+                                        128 ** -0.5)
+        else:
+            s_d = bm // 2
+            t_d = 2 * bm - 2 * s_d
+            nd = lmax // 2
+            kparts, vrows, acc = [], [], 0
+            for j in range(seqs):
+                kp = torch.cat([torch.arange(j * lmax, j * lmax + nd - t_d),
+                                torch.arange(j * lmax + nd + s_d, (j + 1) * lmax)])
+                kparts.append(kp)
+                vrows.append((acc, acc + kp.numel(), j * 2 * bm, (j + 1) * 2 * bm))
+                acc += kp.numel()
+            kpos = torch.cat(kparts).to(dev)
+            vb = torch.tensor(vrows, dtype=torch.int32, device=dev)
+            mask = torch.from_numpy(np.concatenate([_verify_mask(bm, s_d)] * seqs)).to(dev)
+            xv = rnd(2 * bm * seqs, d)
+            k1, v1, ov = rnd(2 * bm * seqs, d), rnd(2 * bm * seqs, d), torch.empty_like(xv)
+            fn = lambda: ops.verify_attn(xv, k1, v1, ov, kc, vc, kpos, mask, vb, 2 * bm, H,  # noqa: E731
+                                         128 ** -0.5, max_keys=lmax)
+    elif name == "mlp":
+        W = rnd(2 * hid, d, std=0.02)
+        fn = lambda: ops.linear_swiglu(x, W)  # noqa: E731
+    elif name in ("attn_out", "ff_out"):
+        k = d if name == "attn_out" else hid
+        a, W, r = rnd(n_rows, k), rnd(d, k, std=0.02), rnd(n_rows, d)
+        fn = lambda: ops.linear(a, W, r)  # noqa: E731
+    else:
+        raise SystemExit(f"unknown kernel {name}")
+    for _ in range(reps):
+        fn()
+    torch.cuda.synchronize()
+    check_device_status()
+    print("ok", name, n_rows, flush=True)
 
 
 def run_kernels_only(seqs: int, w: dict) -> None:

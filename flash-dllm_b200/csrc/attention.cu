@@ -969,8 +969,16 @@ __global__ void __launch_bounds__(kScoreThreads)
   const int64_t ld = seqlen_max;
   const float* c = colsum + static_cast<int64_t>(first) * n_heads * ld + key;
   float acc = 0.f;
-  for (int m = 0; m < n_masked; ++m)
-    for (int h = 0; h < n_heads; ++h) acc += c[(static_cast<int64_t>(m) * n_heads + h) * ld];
+  const int n = n_masked * n_heads;
+  // loads in batches of 8 (independent, in flight together), added in order
+  for (int i0 = 0; i0 < n; i0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = i0 + j < n ? __ldg(c + static_cast<int64_t>(i0 + j) * ld) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (i0 + j < n) acc += v[j];
+  }
   scores[static_cast<int64_t>(b) * ld + key] += acc * score_scale;
 }
 
