@@ -13,7 +13,8 @@ __path__ = [_os.path.join(_os.path.dirname(_os.path.abspath(__file__)), "flash-d
 
 _PUBLIC = ("flash_fused_elastic_cache", "generate_with_Flash_dLLM", "get_rotary_embedding", "make_blocks",
            "LLaDAModelB200", "LLaDAConfigB200", "install_into_reference", "qkv_rope_cache", "verify_qkv",
-           "rmsnorm", "attn_cache", "verify_attn", "plan_cache_attention")
+           "rmsnorm", "attn_cache", "verify_attn", "plan_cache_attention", "from_pretrained", "load_model",
+           "load_tokenizer")
 
 
 def __getattr__(name):
