@@ -3,7 +3,8 @@ random-init LLaDA-8B, sequence-sharded over N GPUs of one node (one process
 per GPU, no collective on the hot path; NCCL only gathers the counters).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
-                    [--workload config4|config3|config3_forced2|config5] [--seqs-per-gpu S]
+                    [--workload config4|config3|config3_forced2|config5] [--scaling weak|strong]
+                    [--seqs-per-gpu S]
 
 Workloads (synthetic prompts uniform over the vocabulary
 minus the mask id, random-init weights N(0, 0.02)):
@@ -13,9 +14,13 @@ minus the mask id, random-init weights N(0, 0.02)):
       at least 2 accepts per step);
   config5: batch 32 prompts of 1536, gen 512, refresh budget 64 (track_num 2),
       Flash-Verify on (2176-slot caches).
-``--seqs-per-gpu S`` fixes the per-GPU batch (global batch S x N: weak
-scaling); otherwise the workload's global batch is split over the GPUs
-(strong scaling).
+Sequences are independent, so N GPUs shard them with no collective on the
+data path.  ``--scaling weak`` (default) gives every rank its own batch of the
+workload's per-GPU size (config4: 8 prompts, the one-GPU configuration;
+config5: 4 prompts, its stated per-GPU share), so the global batch is that
+size x N and per-GPU work is fixed; ``--scaling strong`` splits the
+workload's global batch over the ranks (config4's 8 prompts over 1/2/4/8
+GPUs).  ``--seqs-per-gpu S`` sets the weak per-GPU batch.
 
 A step is one decode iteration on every rank: the Flash-Cache forward, the
 Flash-Verify forward (when on) and the bookkeeping kernels for that rank's
@@ -53,14 +58,14 @@ METRIC = "generated tokens/s (LLaDA-8B, gen 512) at 1/2/4/8 B200; fused-layer us
 MODEL = "LLaDA-8B (random init N(0,0.02))"
 _COMMON = dict(block_length=32, threshold=0.9, mask_num=1, mask_id=126336, eos_id=126081)
 WORKLOADS = {
-    "config4": dict(workload="llada8b_flash_cache_verify_decode", global_batch=8, prompt_len=256, gen_length=512,
-                    gamma=0.8, track_num=1, verify=True, min_keep=1),
-    "config3": dict(workload="llada8b_flash_cache_b1_gen256", global_batch=1, prompt_len=256, gen_length=256,
-                    gamma=0.9, track_num=1, verify=False, min_keep=1),
-    "config3_forced2": dict(workload="llada8b_flash_cache_b1_gen256_forced2", global_batch=1, prompt_len=256,
-                            gen_length=256, gamma=0.9, track_num=1, verify=False, min_keep=2),
-    "config5": dict(workload="llada8b_long_context_verify", global_batch=32, prompt_len=1536, gen_length=512,
-                    gamma=0.8, track_num=2, verify=True, min_keep=1),
+    "config4": dict(workload="llada8b_flash_cache_verify_decode", global_batch=8, per_gpu=8, prompt_len=256,
+                    gen_length=512, gamma=0.8, track_num=1, verify=True, min_keep=1),
+    "config3": dict(workload="llada8b_flash_cache_b1_gen256", global_batch=1, per_gpu=1, prompt_len=256,
+                    gen_length=256, gamma=0.9, track_num=1, verify=False, min_keep=1),
+    "config3_forced2": dict(workload="llada8b_flash_cache_b1_gen256_forced2", global_batch=1, per_gpu=1,
+                            prompt_len=256, gen_length=256, gamma=0.9, track_num=1, verify=False, min_keep=2),
+    "config5": dict(workload="llada8b_long_context_verify", global_batch=32, per_gpu=4, prompt_len=1536,
+                    gen_length=512, gamma=0.8, track_num=2, verify=True, min_keep=1),
 }
 # DRAM bytes (read + write) of one launch, from an ncu capture of that kernel
 # at that row count (the per-kernel summaries give the commands); emitted
@@ -100,28 +105,61 @@ def _prompts(n, length, vocab, mask_id, seed=0):
 
 
 class _Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """Clock and throttle-reason sampling during the timed region: NVML every
+    20 ms (read-only queries), nvidia-smi every 200 ms where NVML is absent."""
+
+    _REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                ("sw_power_cap", 0x4))
 
     def __init__(self, index: int):
-        self.index = index
+        self.index = str(index)  # CUDA ordinal -> the GPU's UUID, which NVML and nvidia-smi both accept
+        try:
+            self.index = "GPU-" + str(torch.cuda.get_device_properties(index).uuid)
+        except Exception:
+            pass
         self.samples = []
         self._stop = threading.Event()
         self._t = None
 
+    def _nvml(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = (pynvml.nvmlDeviceGetHandleByUUID(self.index) if self.index.startswith("GPU-")
+                 else pynvml.nvmlDeviceGetHandleByIndex(int(self.index)))
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def read():
+                mask = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                act = ["Active" if mask & bit else "Not Active" for _, bit in self._REASONS]
+                return [str(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)), str(mx), ""] + act
+            read()
+            return read
+        except Exception:
+            return None
+
     def start(self):
-        def run():
+        read = self._nvml()
+
+        def smi():
             q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
                  "clocks_event_reasons.sw_power_cap")
+            r = subprocess.run(["nvidia-smi", "-i", self.index, f"--query-gpu={q}",
+                                "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+            if r.returncode == 0 and r.stdout.strip():
+                return [v.strip() for v in r.stdout.strip().split(",")]
+            return None
+
+        def run():
             while not self._stop.is_set():
                 try:
-                    r = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                        "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                    if r.returncode == 0 and r.stdout.strip():
-                        self.samples.append([v.strip() for v in r.stdout.strip().split(",")])
+                    v = read() if read else smi()
+                    if v:
+                        self.samples.append(v)
                 except Exception:
                     pass
-                self._stop.wait(0.2)
+                self._stop.wait(0.02 if read else 0.2)
         self._t = threading.Thread(target=run, daemon=True)
         self._t.start()
 
@@ -439,8 +477,8 @@ def run_reference(args):
             times.append(t)
             toks.append(k)
     value = float(sum(toks) / sum(times))
-    weak = args.seqs_per_gpu > 0
-    per = args.seqs_per_gpu if weak else w["global_batch"]
+    weak = args.scaling == "weak"
+    per = (args.seqs_per_gpu or w["per_gpu"]) if weak else w["global_batch"]
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * float(np.mean(times)),
             "higher_is_better": True, "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "fp32",
@@ -458,8 +496,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200")
     ap.add_argument("--workload", default="config4", choices=sorted(WORKLOADS))
+    ap.add_argument("--scaling", default="weak", choices=("weak", "strong"),
+                    help="weak: a fixed batch per GPU (default); strong: the workload's batch split over GPUs")
     ap.add_argument("--seqs-per-gpu", type=int, default=0,
-                    help="fixed sequences per GPU (weak scaling); default: the workload's batch split over GPUs")
+                    help="per-GPU batch under weak scaling (default: the workload's per-GPU size)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-kernels", action="store_true")
@@ -485,10 +525,10 @@ def main():
     import flash_dllm_b200._lib as L
     cfg = LLaDAConfigB200()
     model = LLaDAModelB200.random_init(cfg, device=dev, seed=0)
-    weak = args.seqs_per_gpu > 0
+    weak = args.scaling == "weak"
     from flash_dllm_b200.shard import reduce_counters, shard_range
     if weak:
-        per = args.seqs_per_gpu
+        per = args.seqs_per_gpu or w["per_gpu"]
         prompts = _prompts(per * world, w["prompt_len"], cfg.vocab_size, cfg.mask_token_id)
         mine = prompts[rank * per:(rank + 1) * per]
     else:
