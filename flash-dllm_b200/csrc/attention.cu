@@ -16,11 +16,12 @@
 // pages[b * pages_per_seq + n / 64] * 64 + n % 64.  A 64-key tile is one page,
 // so either way a tile is one pair of TMA boxes.
 //
-// attn_scores: every (item, head) CTA writes the raw-logit column sums of its
-// masked rows into its own slice of a workspace (no atomics); a second small
-// kernel adds them to attn_scores in a fixed order (chunks, then heads), so
-// the scores -- and every refresh decision taken from them -- are the same
-// on every run.
+// attn_scores: every (item, head) CTA adds the raw-logit column sums of its
+// masked rows to a per-sequence accumulator in 2^-32 fixed point (64-bit
+// integer atomics: integer addition does not depend on the order, so the sums
+// -- and every refresh decision taken from them -- are the same on every
+// run); the CTA that arrives last for a sequence converts its accumulator
+// once into attn_scores and leaves it zeroed for the next call.
 #include <cstring>
 
 #include "common.cuh"
@@ -74,7 +75,9 @@ struct AttnParams {
   const int32_t* vblocks;       // verify mode: (k_s, k_e, q_s, q_e) rows
   const int64_t* pos_k;         // verify mode: gathered key slots
   const uint8_t* mask;          // verify mode: [n_blocks*block_rows, block_rows]
-  float* colsum;                // cache mode with scores: [masked item][head][seqlen_max] fp32 column sums
+  unsigned long long* score_acc;  // cache mode with scores: [batch][seqlen_max] fixed-point column sums
+  int32_t* score_cnt;           // cache mode with scores: [batch] arrivals
+  float* scores;                // cache mode: attn_scores (NULL: none)
   const int32_t* pages;         // cache mode, optional: page table [batch][pages_per_seq]
   int32_t* status;
   int64_t n_slots;
@@ -86,6 +89,7 @@ struct AttnParams {
   int32_t seqlen_max;
   int32_t kv_splits;
   int32_t n_items;              // verify mode: n_blocks * row chunks
+  int32_t max_items;            // cache mode: plan entries (capacity) the launch covers
   int32_t block_rows;           // verify mode
   int32_t row_chunks;           // verify mode: ceil(block_rows / 64)
   int32_t n_rows;               // rows of q / o (and of k1 / v1 in verify mode)
@@ -111,15 +115,20 @@ __device__ __forceinline__ int item_row(const Item& it, int r) {
 
 __device__ __forceinline__ bool load_item(const AttnParams& p, bool verify, int item_id, Item& it) {
   if (!verify) {
-    if (item_id >= p.plan[0]) return false;
-    const int32_t* e = p.plan + kPlanHeader + item_id * kPlanItem;
-    it.seq = e[0];
-    it.n_keys = e[1];
-    it.m_start = e[2];
-    it.m_len = e[3];
-    it.t_start = e[4];
-    it.rows = e[3] + e[5];
-    it.mchunk = e[6];
+    // the entry (inside the plan's capacity) and the item count are read
+    // together, then the entry is used only below the count
+    if (item_id >= p.max_items) return false;
+    const int4* e = reinterpret_cast<const int4*>(p.plan + kPlanHeader + item_id * kPlanItem);
+    const int n_items = p.plan[0];
+    const int4 e0 = e[0], e1 = e[1];
+    if (item_id >= n_items) return false;
+    it.seq = e0.x;
+    it.n_keys = e0.y;
+    it.m_start = e0.z;
+    it.m_len = e0.w;
+    it.t_start = e1.x;
+    it.rows = e0.w + e1.y;
+    it.mchunk = e1.z;
     return it.rows > 0;
   }
   if (item_id >= p.n_items) return false;
@@ -183,12 +192,20 @@ __device__ __forceinline__ bool load_item(const AttnParams& p, bool verify, int 
 // of a row only moves (and O is rescaled in TMEM) when a tile raises the row
 // max by more than 2^8, so P stays within bf16 range and O is rarely touched;
 // l and O always share the reference max.
-// Per 64-key tile t of a half (2 K and 2 V stages, 2 S buffers, 2 P buffers):
+// Per 64-key tile t of a half (3 K and 2 V stages, 2 S buffers, 1 P buffer):
 //   producers: K(t) -> k_full, V(t) -> v_full (never waiting on each other)
 //   MMA:       S(t) -> s_full, k_empty;  then PV(t-1) after p_full(t-1) ->
 //              pv_done, v_empty
-//   softmax:   S(t) -> s_empty;  P(t) -> p_full once PV(t-2) freed the buffer
+//   softmax:   S(t) -> s_empty;  P(t) -> p_full once PV(t-1) freed the buffer
 //   scores:    S(t) rows of qbar -> s_empty, column sums to the workspace
+// K(t+3) can only be requested once S(t) is done, and S(t+3) must be done
+// when the softmax reaches tile t+3, so a tile period has to cover a third of
+// (K load latency + S product); with two K stages it was half of it, which
+// set the period (1.15 us per tile measured at full load, against 0.8 us of
+// softmax).  The third K stage is paid for with the second P buffer, which
+// bought little: the softmax of tile t computes its exponentials before it
+// needs PV(t-1) done.  V has slack: V(t+2) is requested when PV(t) is done
+// and needed a whole softmax period after PV(t+1).
 // ---------------------------------------------------------------------------
 constexpr int kTcWarps = 12;
 constexpr int kTcThreads = kTcWarps * 32;
@@ -196,29 +213,39 @@ constexpr uint32_t kTcTmemCols = 512;
 constexpr float kTcRescaleThreshold = 8.f;  // log2 units
 constexpr int kTcPBytes = kItemRows * 128;  // 64 rows x 64 keys
 constexpr int kTcWin = 128 * 128;           // bytes an M=128 A operand reads from its base
-// Half 0 (query rows 0-63, qbar rows 64/65): Q halves of 72 rows (9 KB) each
-constexpr int kH0Q0 = 0, kH0Q1 = 9 * 1024, kH0P = 18 * 1024, kH0K = 34 * 1024, kH0V = 66 * 1024,
-              kH0Scr = 98 * 1024, kH0Bar = kH0Scr + 256, kH0End = 99 * 1024;
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
+// Half 0 (query rows 0-63, qbar rows 64/65): Q halves of 72 rows (9 KB) each,
+// one P buffer, the K and V stages.
+constexpr int kH0Q0 = 0, kH0Q1 = 9 * 1024, kH0P = 18 * 1024, kH0K = 26 * 1024,
+              kH0V = kH0K + kKStages * kTileBytes, kH0End = kH0V + kVStages * kTileBytes;
 // Half 1 (qbar rows 0/1, query rows 64-127): Q windows of 16 KB each, the
-// query rows in their second 8 KB; P buffers are read from 8 KB before them.
+// query rows in their second 8 KB; the P buffer is read from 8 KB before it.
+// Both halves' score scratch and barriers sit in rows 8-23 of half 1's first
+// Q window, which carry nothing (only its rows 0-7 and 64-127 hold data).
 constexpr int kH1Base = kH0End;
-constexpr int kH1Q0 = kH1Base, kH1Q1 = kH1Base + 16 * 1024, kH1P = kH1Base + 32 * 1024,
-              kH1K = kH1Base + 48 * 1024, kH1V = kH1Base + 80 * 1024, kH1Scr = kH1Base + 112 * 1024,
-              kH1Bar = kH1Scr + 256, kH1End = kH1Base + 113 * 1024;
-constexpr int kTcSmem = 1024 + kH1End;
-static_assert(kH0Q0 + kTcWin <= kH0End && kH0Q1 + kTcWin <= kH1End && kH0P + kTcPBytes + kTcWin <= kH1End,
+constexpr int kH1Q0 = kH1Base, kH1Scr = kH1Base + 1024, kH1Bar = kH1Scr + 512, kH0Scr = kH1Base + 2 * 1024,
+              kH0Bar = kH0Scr + 512, kH1Q1 = kH1Base + 16 * 1024, kH1P = kH1Base + 32 * 1024,
+              kH1K = kH1Base + 40 * 1024, kH1V = kH1K + kKStages * kTileBytes,
+              kH1End = kH1V + kVStages * kTileBytes;
+constexpr int kTcSmem = 1024 + kH1End;  // + alignment of the base to 1024 bytes
+static_assert(kH0Q0 + kTcWin <= kH1End && kH0Q1 + kTcWin <= kH1End && kH0P + kTcWin <= kH1End,
               "half-0 operand windows inside shared memory");
-static_assert(kH1P - 8 * 1024 >= 0 && kH1P + kTcPBytes + 8 * 1024 <= kH1End && kH1Q1 + kTcWin <= kH1End,
+static_assert(kH1P - 8 * 1024 >= kH1Q1 && kH1P + kTcPBytes <= kH1K && kH1Q1 + kTcWin <= kH1End,
               "half-1 operand windows inside shared memory");
+static_assert(kH0P + kTcPBytes <= kH0K && kH1Scr >= kH1Q0 + 1024 && kH1Bar + 512 <= kH0Scr &&
+                  kH0Bar + 512 <= kH1Q0 + 8 * 1024,
+              "scratch and barriers outside the data rows");
 static_assert(kTcSmem <= 227 * 1024, "shared memory");
+static_assert(kKStages * kTileBytes >= kItemRows * kHD * 4, "a key slice's fp32 O rows fit the K stages");
 
 struct TcHalf {
   uint32_t row_lane;   // TMEM lane / operand row of query row 0
   uint32_t qbar_lane;  // TMEM lane / operand row of qbar hi
   uint8_t* q_win0;     // S operand windows (64-dim halves)
   uint8_t* q_win1;
-  uint8_t* p_row0;     // P buffer 0: address of query row 0's P row (+ b * kTcPBytes)
-  uint8_t* p_win;      // P buffer 0 operand window (+ b * kTcPBytes)
+  uint8_t* p_row0;     // P buffer: address of query row 0's P row
+  uint8_t* p_win;      // P buffer operand window
   uint8_t* k;          // K stage 0 (+ s * kTileBytes)
   uint8_t* v;          // V stage 0 (+ s * kTileBytes)
   float* scr;
@@ -327,15 +354,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                : ((warp & 1) ? kMma : kScores);
   const int h = warp < 4 ? (warp >> 1) : warp >= 8 ? ((warp >> 1) & 1) : (warp == 4 || warp == 7) ? 1 : 0;
   const TcHalf H = tc_half(smem, h);
-  uint64_t* k_full = H.bar;
-  uint64_t* k_empty = H.bar + 2;
-  uint64_t* v_full = H.bar + 4;
-  uint64_t* v_empty = H.bar + 6;
-  uint64_t* s_full = H.bar + 8;
-  uint64_t* s_empty = H.bar + 10;
-  uint64_t* p_full = H.bar + 12;
-  uint64_t* pv_done = H.bar + 14;
-  uint64_t* mma_done = H.bar + 16;
+  uint64_t* k_full = H.bar;                                // [kKStages]
+  uint64_t* k_empty = k_full + kKStages;                   // [kKStages]
+  uint64_t* v_full = k_empty + kKStages;                   // [kVStages]
+  uint64_t* v_empty = v_full + kVStages;                   // [kVStages]
+  uint64_t* s_full = v_empty + kVStages;                   // [2]
+  uint64_t* s_empty = s_full + 2;                          // [2]
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* pv_done = p_full + 1;
+  uint64_t* mma_done = pv_done + 1;
+  static_assert(2 * (kKStages + kVStages) + 7 <= 17, "barriers below the fail flag");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kH0Bar + 18 * 8);
   volatile int32_t* fail = reinterpret_cast<volatile int32_t*>(H.bar + 17);
 
@@ -356,7 +384,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int nt_blk = (kVerify && split == p.kv_splits - 1) ? (it.blk_rows + kKeyTile - 1) / kKeyTile : 0;
     n_tiles = nt_cache + nt_blk;
   }
-  const bool scores_on = !kVerify && has_item && p.colsum != nullptr && it.m_len > 0 && it.mchunk >= 0;
+  const bool scores_on = !kVerify && has_item && p.scores != nullptr && it.m_len > 0 && it.mchunk >= 0;
   const int64_t d = p.d_model;
   {
     // the CTA exits only when neither half has an item
@@ -366,16 +394,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 
   if (role == kMma && lane == 0) {
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], scores_on ? 3 : 2);
-      mbar_init(&p_full[s], 2);
-      mbar_init(&pv_done[s], 1);
     }
+    mbar_init(p_full, 2);
+    mbar_init(pv_done, 1);
     mbar_init(mma_done, 1);
     *fail = 0;
     fence_barrier_init();
@@ -391,6 +423,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   }
+  // barriers and TMEM are ready: the producers start loading K/V at once,
+  // while warps 0-7 fill the Q operands
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   if (warp < 8) {
     // operand fill of half f by threads [128 f, 128 f + 128): query rows (rows
     // past the item zero), qbar hi / lo, the other rows of qbar's 8-row atom
@@ -417,30 +454,50 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int hh = tid >> 6, rr = F.qbar_lane + ((tid >> 3) & 7), ch = tid & 7;
       *reinterpret_cast<uint4*>(win_chunk(hh ? F.q_win1 : F.q_win0, rr, ch)) = make_uint4(0, 0, 0, 0);
     }
-    const bool f_scores = !kVerify && f_has && p.colsum != nullptr && fi.m_len > 0 && fi.mchunk >= 0;
+    const bool f_scores = !kVerify && f_has && p.scores != nullptr && fi.m_len > 0 && fi.mchunk >= 0;
     if (f_scores) {
-      // qbar dim = tid: fp32 sum over the masked rows (the item's first m_len
-      // rows) -> bf16 hi (row qbar_lane) and lo (row qbar_lane + 1)
+      // qbar = fp32 sum of the masked rows (the item's first m_len rows) ->
+      // bf16 hi (row qbar_lane) and lo (row qbar_lane + 1).  Every thread
+      // adds its own loaded rows (8 dims of chunk tid & 15), lanes 16 apart
+      // combine, then the four warps' partials are added in warp order
+      // through the P buffer (unused until the first softmax): a fixed order.
+      float part[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) part[e] = 0.f;
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        if ((tid >> 4) + 8 * k < fi.m_len) {
+          const __nv_bfloat162* pv = reinterpret_cast<const __nv_bfloat162*>(&v[k]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 x = __bfloat1622float2(pv[e]);
+            part[2 * e] += x.x;
+            part[2 * e + 1] += x.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) part[e] += __shfl_xor_sync(0xffffffffu, part[e], 16);
+      float* red = reinterpret_cast<float*>(F.p_row0);  // [4 warps][128 dims]
+      if ((tid & 31) < 16) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) red[(tid >> 5) * kHD + (tid & 15) * 8 + e] = part[e];
+      }
       if (f == 0)
         asm volatile("bar.sync 1, 128;" ::: "memory");
       else
         asm volatile("bar.sync 2, 128;" ::: "memory");
       const int dim = tid, c = (dim & 63) >> 3;
       uint8_t* win = (dim >> 6) ? F.q_win1 : F.q_win0;
-      float acc = 0.f;
-      for (int r = 0; r < fi.m_len; ++r)
-        acc += __bfloat162float(
-            *reinterpret_cast<const __nv_bfloat16*>(win_chunk(win, F.row_lane + r, c) + (dim & 7) * 2));
+      const float acc = ((red[dim] + red[kHD + dim]) + red[2 * kHD + dim]) + red[3 * kHD + dim];
       const __nv_bfloat16 hi = __float2bfloat16_rn(acc);
       const __nv_bfloat16 lo = __float2bfloat16_rn(acc - __bfloat162float(hi));
       *reinterpret_cast<__nv_bfloat16*>(win_chunk(win, F.qbar_lane, c) + (dim & 7) * 2) = hi;
       *reinterpret_cast<__nv_bfloat16*>(win_chunk(win, F.qbar_lane + 1, c) + (dim & 7) * 2) = lo;
     }
     fence_proxy_async_smem();
+    asm volatile("bar.sync 3, 256;" ::: "memory");  // warps 0-7: Q in place for the S products
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
   const uint32_t tmem = *tmem_slot + H.col;
 
   if ((role == kProdK || role == kProdV) && !kVerify) {
@@ -450,9 +507,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint64_t* full = is_k ? k_full : v_full;
       uint64_t* empty = is_k ? k_empty : v_empty;
       const CUtensorMap* map = is_k ? &map_k : &map_v;
+      const int n_st = is_k ? kKStages : kVStages;
       for (int t = 0; t < n_tiles; ++t) {
-        const int s = t & 1;
-        if (t >= 2 && !mbar_wait(&empty[s], ((t - 2) >> 1) & 1, p.status, kAttnKernelId)) {
+        const int s = t % n_st;
+        if (t >= n_st && !mbar_wait(&empty[s], ((t - n_st) / n_st) & 1, p.status, kAttnKernelId)) {
           *fail = 1;
           break;
         }
@@ -486,10 +544,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const bool is_k = role == kProdK;
     uint64_t* full = is_k ? k_full : v_full;
     uint64_t* empty = is_k ? k_empty : v_empty;
+    const int n_st = is_k ? kKStages : kVStages;
     bool ok = true;
-    int pending = -1;  // gathered tile not yet published
+    int pending = -1;  // stage of the gathered tile not yet published
+    int s = n_st - 1, use = -1;  // stage of tile t, and how often it was filled before
     for (int t = 0; t < n_tiles; ++t) {
-      const int s = t & 1;
+      if (++s == n_st) {
+        s = 0;
+        ++use;
+      }
       // the tile's key rows are read before waiting for its stage, so the
       // position loads overlap the wait
       const bool blk = t >= nt_cache;
@@ -510,7 +573,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         src_row[hh] = row;
       }
-      if (t >= 2 && !mbar_wait(&empty[s], ((t - 2) >> 1) & 1, p.status, kAttnKernelId)) {
+      if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, p.status, kAttnKernelId)) {
         ok = false;
         break;
       }
@@ -531,7 +594,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           asm volatile("cp.async.wait_group 0;" ::: "memory");
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&full[pending & 1]);
+          if (lane == 0) mbar_arrive(&full[pending]);
           pending = -1;
         }
         if (lane == 0) {
@@ -558,14 +621,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         asm volatile("cp.async.wait_group 1;" ::: "memory");
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full[pending & 1]);
+        if (lane == 0) mbar_arrive(&full[pending]);
       }
-      pending = t;
+      pending = s;
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     fence_proxy_async_smem();
     __syncwarp();
-    if (ok && pending >= 0 && lane == 0) mbar_arrive(&full[pending & 1]);
+    if (ok && pending >= 0 && lane == 0) mbar_arrive(&full[pending]);
     if (!ok) *fail = 1;
   } else if (role == kMma) {
     // ------------------------------------------------------------ MMA ----
@@ -575,34 +638,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // descriptors of the operand bases; +16 B adds 1 to the start field
       const uint64_t dq0 = umma_desc_kmajor_sw128(smem_u32(H.q_win0));
       const uint64_t dq1 = umma_desc_kmajor_sw128(smem_u32(H.q_win1));
+      const uint64_t pa = umma_desc_kmajor_sw128(smem_u32(H.p_win));
       auto pv = [&](int u) -> bool {
-        const int b = u & 1;
-        if (!mbar_wait(&p_full[b], (u >> 1) & 1, p.status, kAttnKernelId)) return false;
-        if (!mbar_wait(&v_full[b], (u >> 1) & 1, p.status, kAttnKernelId)) return false;
+        const int vs = u % kVStages;
+        if (!mbar_wait(p_full, u & 1, p.status, kAttnKernelId)) return false;
+        if (!mbar_wait(&v_full[vs], (u / kVStages) & 1, p.status, kAttnKernelId)) return false;
         tc_fence_after();
-        const uint64_t pa = umma_desc_kmajor_sw128(smem_u32(H.p_win + b * kTcPBytes));
-        const uint64_t va = umma_desc_mnmajor_sw128(smem_u32(H.v + b * kTileBytes), kHalfBytes);
+        const uint64_t va = umma_desc_mnmajor_sw128(smem_u32(H.v + vs * kTileBytes), kHalfBytes);
 #pragma unroll
         for (int kk = 0; kk < kKeyTile / 16; ++kk)
           umma_bf16(tmem + 128, pa + (kk * 32 >> 4), va + (kk * 2048 >> 4), idesc_pv, (u > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&pv_done[b]);
-        umma_commit(&v_empty[b]);
+        umma_commit(pv_done);
+        umma_commit(&v_empty[vs]);
         return true;
       };
       bool ok = true;
       for (int t = 0; t < n_tiles && ok; ++t) {
-        const int s = t & 1;
-        ok = mbar_wait(&k_full[s], (t >> 1) & 1, p.status, kAttnKernelId) &&
+        const int s = t & 1;  // S buffer
+        const int ks = t % kKStages;
+        ok = mbar_wait(&k_full[ks], (t / kKStages) & 1, p.status, kAttnKernelId) &&
              (t < 2 || mbar_wait(&s_empty[s], ((t - 2) >> 1) & 1, p.status, kAttnKernelId));
         if (!ok) break;
         tc_fence_after();
-        const uint64_t ka = umma_desc_kmajor_sw128(smem_u32(H.k + s * kTileBytes));
+        const uint64_t ka = umma_desc_kmajor_sw128(smem_u32(H.k + ks * kTileBytes));
 #pragma unroll
         for (int kk = 0; kk < kHD / 16; ++kk)
           umma_bf16(tmem + kKeyTile * s, ((kk >> 2) ? dq1 : dq0) + ((kk & 3) * 32 >> 4),
                     ka + (((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4), idesc_s, kk > 0 ? 1u : 0u);
         umma_commit(&s_full[s]);
-        umma_commit(&k_empty[s]);
+        umma_commit(&k_empty[ks]);
         if (t >= 1) ok = pv(t - 1);
       }
       if (ok && n_tiles > 0) ok = pv(n_tiles - 1);
@@ -614,10 +678,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (role == kScores) {
     // ------------------------------------------------------- scores ----
     if (scores_on) {
-      // this (item, head)'s own row of column sums: written, never accumulated
-      float* srow = p.colsum + (static_cast<int64_t>(it.mchunk) * p.n_heads + head) *
-                                   static_cast<int64_t>(p.seqlen_max);
-      const uint32_t taddr = tmem + (H.qbar_lane << 16);  // lanes qbar, qbar+1 = hi, lo
+      // S rows qbar (hi) and qbar + 1 (lo) are this warp's lanes 0 and 1:
+      // they stage the 64 column values of a tile, every lane then adds hi +
+      // lo of two columns to the sequence's fixed-point accumulator
+      unsigned long long* acc = p.score_acc + static_cast<int64_t>(it.seq) * p.seqlen_max;
+      const uint32_t taddr = tmem + (H.qbar_lane << 16);
+      bool range_ok = true;
       for (int t = 0; t < n_tiles; ++t) {
         const int b = t & 1;
         if (!mbar_wait(&s_full[b], (t >> 1) & 1, p.status, kAttnKernelId)) {
@@ -631,19 +697,59 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty[b]);
-#pragma unroll
-        for (int j = 0; j < 64; ++j) sc[j] += __shfl_down_sync(0xffffffffu, sc[j], 1);  // hi + lo
-        if (lane == 0) {
+        if (lane < 2) {
 #pragma unroll
           for (int j = 0; j < 64; j += 4)
-            *reinterpret_cast<float4*>(H.scr + j) = make_float4(sc[j], sc[j + 1], sc[j + 2], sc[j + 3]);
+            *reinterpret_cast<float4*>(H.scr + 64 * lane + j) = make_float4(sc[j], sc[j + 1], sc[j + 2], sc[j + 3]);
         }
         __syncwarp();
         const int n0 = c0 + t * kKeyTile;
         const int n_valid = c1 - n0;
-        if (lane < n_valid) srow[n0 + lane] = H.scr[lane];
-        if (lane + 32 < n_valid) srow[n0 + lane + 32] = H.scr[lane + 32];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int j = lane + 32 * hh;
+          if (j < n_valid) {
+            const float x = H.scr[j] + H.scr[64 + j];
+            // |x| < 2^24: x * 2^32 is exact in fp32 and up to 128 such terms
+            // per key stay inside int64
+            const bool in_range = fabsf(x) < 16777216.f;  // false for NaN / inf
+            range_ok &= in_range;
+            atomicAdd(acc + n0 + j,
+                      static_cast<unsigned long long>(in_range ? __float2ll_rn(x * 4294967296.f) : 0ll));
+          }
+        }
         __syncwarp();
+      }
+      if (!__all_sync(0xffffffffu, range_ok) && lane == 0) report(p.status, FDLLM_ERR_RANGE, it.seq, kAttnKernelId);
+      // arrival: the last (item, head, split) of the sequence converts
+      const int32_t* sq = p.plan + p.plan[3] + kPlanSeq * it.seq;
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        const int expected = sq[1] * p.n_heads * p.kv_splits;
+        last = atomicAdd(p.score_cnt + it.seq, 1) == expected - 1;
+        if (last) p.score_cnt[it.seq] = 0;
+      }
+      if (__shfl_sync(0xffffffffu, last, 0)) {
+        __threadfence();
+        const int k_end = min(sq[2], p.seqlen_max);
+        float* dst = p.scores + static_cast<int64_t>(it.seq) * p.seqlen_max;
+        for (int n0 = 0; n0 < k_end; n0 += 32 * 4) {
+          unsigned long long v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {  // read and zero, four in flight
+            const int n = n0 + lane + 32 * u;
+            v[u] = n < k_end ? atomicExch(acc + n, 0ull) : 0ull;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int n = n0 + lane + 32 * u;
+            if (n < k_end)
+              dst[n] += static_cast<float>(static_cast<double>(static_cast<long long>(v[u])) * 2.3283064365386963e-10) *
+                        p.score_scale;
+          }
+        }
       }
     }
   } else {
@@ -713,7 +819,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const float alpha = need ? exp2f(m_used - m_new) : 1.f;  // m_used = -inf -> 0
       // O holds PV(0..t-1): rescale it when a row of the warp moves its max
       if (__any_sync(0xffffffffu, need) && t > 0) {
-        ok = mbar_wait(&pv_done[(t - 1) & 1], ((t - 1) >> 1) & 1, p.status, kAttnKernelId);
+        ok = mbar_wait(pv_done, (t - 1) & 1, p.status, kAttnKernelId);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll 1
@@ -745,12 +851,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int k = 0; k < i; ++k) ps[k] += ps[k + i];
       l += ps[0];
-      // P buffer b was last read by PV(t-2)
-      if (t >= 2) {
-        ok = mbar_wait(&pv_done[b], ((t - 2) >> 1) & 1, p.status, kAttnKernelId);
+      // the P buffer was last read by PV(t-1)
+      if (t >= 1) {
+        ok = mbar_wait(pv_done, (t - 1) & 1, p.status, kAttnKernelId);
         if (!ok) break;
       }
-      uint8_t* prow = H.p_row0 + b * kTcPBytes + r * 128;
+      // (the row address is formed per tile: hoisted out of the loop, the
+      // 64-bit pointer would hold two registers across it and spill)
+      int zero;
+      asm volatile("mov.b32 %0, 0;" : "=r"(zero));
+      uint8_t* prow = H.p_row0 + zero + r * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c)
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
@@ -759,23 +869,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (!kVerify && !full) {
         // TMA brought whole rows past the end of this key range: zero their V
         // so 0-probability keys cannot inject non-finite cache contents.
-        ok = mbar_wait(&v_full[b], (t >> 1) & 1, p.status, kAttnKernelId);
+        ok = mbar_wait(&v_full[t % kVStages], (t / kVStages) & 1, p.status, kAttnKernelId);
         if (!ok) break;
         for (int idx = r; idx < (kKeyTile - n_valid) * 16; idx += 64) {
           const int key = n_valid + idx / 16, chunk = idx % 16;
-          *reinterpret_cast<uint4*>(H.v + b * kTileBytes + tile_off(key, chunk)) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(H.v + (t % kVStages) * kTileBytes + tile_off(key, chunk)) =
+              make_uint4(0, 0, 0, 0);
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (lane == 0) mbar_arrive(p_full);
     }
     if (!ok) *fail = 1;
 
     // ------------------------------------------------------ epilogue ----
-    const bool have_o = ok && n_tiles > 0 &&
-                        mbar_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, p.status, kAttnKernelId);
+    const bool have_o = ok && n_tiles > 0 && mbar_wait(pv_done, (n_tiles - 1) & 1, p.status, kAttnKernelId);
     if (have_o) tc_fence_after();
     if (has_item) {
       const int64_t grow = row_ok ? item_row(it, r) : 0;
@@ -948,49 +1058,19 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* __res
   }
 }
 
-// ------------------------------------------------- score reduction ----
-// attn_scores[b * seqlen_max + n] += score_scale * (sum over the masked items
-// of sequence b, in item order, of the sum over heads, in head order, of the
-// column sums the attention kernel wrote).  One thread per key; a fixed
-// order, so the result does not depend on which CTAs finished first.
-// ref llada/flash_cache_triton.py:614-615 (attn_scores += S.mean((0, 1))).
-constexpr int kScoreThreads = 256;
-
-__global__ void __launch_bounds__(kScoreThreads)
-    scores_reduce_kernel(const int32_t* __restrict__ plan, const float* __restrict__ colsum,
-                         float* __restrict__ scores, float score_scale, int n_heads, int seqlen_max) {
-  pdl_wait();  // the column sums come from the attention kernel before
-  const int b = blockIdx.y;
-  if (b >= plan[1]) return;
-  const int32_t* sq = plan + plan[3] + kPlanSeq * b;
-  const int first = sq[0], n_masked = sq[1], k_end = sq[2];
-  const int key = blockIdx.x * kScoreThreads + threadIdx.x;
-  if (n_masked <= 0 || key >= k_end) return;
-  const int64_t ld = seqlen_max;
-  const float* c = colsum + static_cast<int64_t>(first) * n_heads * ld + key;
-  float acc = 0.f;
-  const int n = n_masked * n_heads;
-  // loads in batches of 8 (independent, in flight together), added in order
-  for (int i0 = 0; i0 < n; i0 += 8) {
-    float v[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = i0 + j < n ? __ldg(c + static_cast<int64_t>(i0 + j) * ld) : 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (i0 + j < n) acc += v[j];
-  }
-  scores[static_cast<int64_t>(b) * ld + key] += acc * score_scale;
-}
-
 namespace {
 
 int plan_capacity(int32_t n_rows, int32_t batch) { return (n_rows + kItemRows - 1) / kItemRows + batch; }
 
-// Workspace of fdllm_attn_cache with scores: one row of column sums per
-// (masked item, head); the masked items are at most the plan's capacity.
+// Workspace of fdllm_attn_cache with scores: a fixed-point accumulator row
+// per sequence and an arrival counter per sequence (the batch is at most the
+// plan's capacity).
+size_t attn_acc_bytes(int32_t items, int32_t seqlen_max) {
+  return align_up(static_cast<size_t>(items) * seqlen_max * sizeof(unsigned long long), 256);
+}
 size_t attn_ws_bytes(int32_t items, int32_t heads, int32_t seqlen_max) {
   if (items <= 0 || heads <= 0 || seqlen_max <= 0) return 256;
-  return align_up(static_cast<size_t>(items) * heads * seqlen_max * sizeof(float), 256);
+  return attn_acc_bytes(items, seqlen_max) + align_up(static_cast<size_t>(items) * sizeof(int32_t), 256);
 }
 
 // Key splits the tcgen05 kernel runs: its cluster merge takes 1, 2, 4 or 8
@@ -1073,7 +1153,8 @@ int fdllm_attn_cache(const void* q, void* o, const void* k_cache, const void* v_
   for (const void* x : ptrs)
     if (x == nullptr || !aligned16(x)) return FDLLM_ERR_ARG;
   if (attn_scores != nullptr &&
-      (workspace == nullptr || workspace_bytes < attn_ws_bytes(max_items, n_heads, seqlen_max)))
+      (workspace == nullptr || !aligned16(workspace) ||
+       workspace_bytes < attn_ws_bytes(max_items, n_heads, seqlen_max)))
     return FDLLM_ERR_WORKSPACE;
   CUtensorMap mk, mv;
   int rc;
@@ -1085,7 +1166,11 @@ int fdllm_attn_cache(const void* q, void* o, const void* k_cache, const void* v_
   p.kc = static_cast<const __nv_bfloat16*>(k_cache);
   p.vc = static_cast<const __nv_bfloat16*>(v_cache);
   p.plan = static_cast<const int32_t*>(plan);
-  p.colsum = attn_scores != nullptr ? static_cast<float*>(workspace) : nullptr;
+  p.scores = attn_scores;
+  if (attn_scores != nullptr) {
+    p.score_acc = static_cast<unsigned long long*>(workspace);
+    p.score_cnt = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + attn_acc_bytes(max_items, seqlen_max));
+  }
   p.pages = page_table;
   p.pages_per_seq = page_table != nullptr ? pages_per_seq : 0;
   p.status = status_ptr();
@@ -1096,14 +1181,8 @@ int fdllm_attn_cache(const void* q, void* o, const void* k_cache, const void* v_
   p.n_heads = n_heads;
   p.seqlen_max = seqlen_max;
   p.kv_splits = kv_splits;
-  if ((rc = launch_attn<false>(mk, mv, mk, mv, p, max_items, stream)) != FDLLM_OK) return rc;
-  if (attn_scores == nullptr) return FDLLM_OK;
-  const dim3 sgrid(static_cast<unsigned>((seqlen_max + kScoreThreads - 1) / kScoreThreads),
-                   static_cast<unsigned>(max_items), 1);
-  if (launch_ex(scores_reduce_kernel, sgrid, dim3(kScoreThreads), 0, stream, 1, pdl_enabled(), p.plan,
-                static_cast<const float*>(p.colsum), attn_scores, score_scale, n_heads, seqlen_max) != cudaSuccess)
-    return FDLLM_ERR_CUDA;
-  return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
+  p.max_items = max_items;
+  return launch_attn<false>(mk, mv, mk, mv, p, max_items, stream);
 }
 
 int fdllm_verify_attn(const void* q1, const void* k1, const void* v1, void* o, const void* k_cache,

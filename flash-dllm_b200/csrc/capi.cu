@@ -131,6 +131,7 @@ const char* fdllm_error_string(int code) {
     case FDLLM_ERR_WORKSPACE: return "workspace too small";
     case FDLLM_ERR_DRIVER: return "TMA descriptor encode failed";
     case FDLLM_ERR_SCRATCH_LIMIT: return "request exceeds the fixed scratch of the no-allocation entry point";
+    case FDLLM_ERR_RANGE: return "attention-score column sum out of range (device)";
     default: return "unknown status";
   }
 }

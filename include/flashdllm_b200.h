@@ -40,6 +40,7 @@ extern "C" {
 #define FDLLM_ERR_WORKSPACE 6 /* workspace too small */
 #define FDLLM_ERR_DRIVER 7    /* TMA descriptor encode unavailable or failed */
 #define FDLLM_ERR_SCRATCH_LIMIT 8 /* request needs more scratch than the library's fixed array holds */
+#define FDLLM_ERR_RANGE 9     /* device: an attention-score column sum non-finite or beyond 2^24 in magnitude */
 
 /* Library version string. */
 const char* fdllm_version(void);
@@ -175,9 +176,10 @@ int fdllm_plan_cache_attention(const int64_t* masked_blocks, int32_t n_masked, c
                                int32_t n_tracked, int32_t n_rows, int32_t batch_size, int32_t block_m,
                                int32_t seqlen_max, void* plan, size_t plan_bytes, cudaStream_t stream);
 
-/* Workspace (bytes) fdllm_attn_cache needs when it accumulates attn_scores: one fp32 row of
- * seqlen_max column sums per (masked work item, head), max_items = fdllm_attn_plan_capacity(...).
- * Needs no zero-fill: every value read is written by the same call. */
+/* Workspace (bytes) fdllm_attn_cache needs when it accumulates attn_scores: a 64-bit fixed-point
+ * accumulator of seqlen_max entries and an arrival counter per sequence (max_items =
+ * fdllm_attn_plan_capacity(...) bounds the batch).  Zero-filled once before first use; every call
+ * leaves it zeroed again (after a call whose device status reported an error, zero it again). */
 size_t fdllm_attn_workspace_bytes(int32_t max_items, int32_t n_heads, int32_t seqlen_max);
 
 /* Block-table scheduled attention over the KV cache for masked + tracked rows.
@@ -191,8 +193,11 @@ size_t fdllm_attn_workspace_bytes(int32_t max_items, int32_t n_heads, int32_t se
  *   attn_scores  fp32 [batch*seqlen_max] (logical slots) or NULL: when given, for every key n of
  *              sequence b, attn_scores[b*seqlen_max + n] += score_scale * sum over masked rows and
  *              heads of the raw (unscaled) q.k logit -- the reference's S tensor + S.mean((0,1))
- *              fused.  The sum is taken in a fixed order (a second kernel adds per-head column sums
- *              from the workspace), so the scores are the same on every run.
+ *              fused.  Per (item, head) column sums (fp32, from the tensor cores) are added in
+ *              2^-32 fixed point with 64-bit integer atomics -- exact and order-independent, so the
+ *              scores are the same on every run -- and converted once per sequence by the last
+ *              CTA to finish it.  A column sum that is non-finite or reaches 2^24 in magnitude is
+ *              reported as FDLLM_ERR_RANGE (and left out).
  *   kv_splits  split of each item's key range over CTAs: 1 = none; 2, 4 or 8 (other counts round
  *              down) run as one cluster of CTAs per item pair, merged in distributed shared memory
  * ref llada/flash_cache_triton.py:103-252 (_flash_masked_attention_fwd, _flash_tracked_attention_fwd)

@@ -4,7 +4,7 @@ attention against the CPU oracle (the reference kernels' semantics, bf16
 inputs, P rounded to bf16 like the reference).  Outputs: max |cuda - oracle| /
 max |oracle| <= 2e-2; accumulated scores: <= 1e-3 (fp32 sums of the same
 bf16 products in a different order).  The scores must also be bit-identical
-from one run to the next (fixed-order reduction)."""
+from one run to the next (order-independent fixed-point sums)."""
 import numpy as np
 import pytest
 import torch
@@ -137,10 +137,12 @@ def test_cache_attention_config2_paged(kv_splits):
 
 
 def test_scores_are_reproducible():
-    """The same forward twice (and once more with the keys split over a
-    cluster) gives bit-identical attn_scores: the column sums are reduced in a
-    fixed order, so refresh decisions taken from them do not vary run to run.
-    Scores accumulate on top of earlier values, as across layers."""
+    """The same forward three times and twice more with the keys split over a
+    cluster gives bit-identical attn_scores: the column sums are added as
+    integers (2^-32 fixed point), exact in any order, so neither the order in
+    which CTAs finish nor the key split changes a score, and refresh decisions
+    taken from them do not vary run to run.  Scores accumulate on top of
+    earlier values, as across layers."""
     B, bm, lmax, H, k_ends, tracked, _ = _config2(seed=6)
     q, kc, vc, mb, tb, n = _cache_inputs(k_ends, [bm] * B, tracked, H * 128, lmax, bm, seed=13)
     sc0 = torch.randn(B * lmax, generator=torch.Generator().manual_seed(2))
@@ -148,9 +150,25 @@ def test_scores_are_reproducible():
     for o, sc in runs[1:3]:
         assert torch.equal(sc, runs[0][1])
         assert torch.equal(o, runs[0][0])
-    assert torch.equal(runs[4][1], runs[3][1])
+    assert torch.equal(runs[3][1], runs[0][1]) and torch.equal(runs[4][1], runs[0][1])
     oo, so = _oracle_cache(q, kc, vc, mb, tb, lmax, bm, H, B)
     assert _rel(runs[0][1] - sc0.cuda(), so) <= SCORE_TOL
+
+
+def test_out_of_range_scores_are_reported():
+    """A masked-row column sum beyond the fixed-point range (|sum| >= 2^24;
+    here queries scaled by 1e5) is reported as FDLLM_ERR_RANGE after the
+    call, the output rows are still written, and the score workspace is
+    zeroed again so the next call is exact."""
+    from flash_dllm_b200._lib import FdllmError
+    B, bm, lmax, H, k_ends, tracked, _ = _config2(seed=4)
+    q, kc, vc, mb, tb, n = _cache_inputs(k_ends, [bm] * B, tracked, H * 128, lmax, bm, seed=15)
+    with pytest.raises(FdllmError) as e:
+        _run_cache((q.float() * 1e5).bfloat16(), kc, vc, mb, tb, n, lmax, bm, H, B, 1)
+    assert e.value.code == 9
+    o, sc = _run_cache(q, kc, vc, mb, tb, n, lmax, bm, H, B, 1)
+    oo, so = _oracle_cache(q, kc, vc, mb, tb, lmax, bm, H, B)
+    assert _rel(o, oo) <= TOL and _rel(sc, so) <= SCORE_TOL
 
 
 def test_cache_attention_config5_shape():

@@ -46,8 +46,9 @@ def test_host_side_queries_and_checks(lib):
     assert L.fdllm_error_string(0) == b"ok"
     assert L.fdllm_attn_plan_capacity(512, 8) == 512 // 64 + 8
     assert L.fdllm_attn_plan_bytes(512, 8) >= 4 * (8 + 16 * 8 + 3 * 8)
-    # scores workspace: one fp32 row of seqlen_max per (item, head)
-    assert L.fdllm_attn_workspace_bytes(16, 32, 896) >= 16 * 32 * 896 * 4
+    # scores workspace: a 64-bit accumulator row and a counter per sequence
+    assert L.fdllm_attn_workspace_bytes(16, 32, 896) >= 16 * 896 * 8 + 16 * 4
+    assert L.fdllm_error_string(9).decode().startswith("attention-score column sum out of range")
     # invalid arguments are refused before anything is launched
     assert L.fdllm_attn_cache(None, None, None, None, None, 1, None, 1.0, 4096, 0, 896, 7168, 0.1, 1, None, 0,
                               None, 0, None) == 1
