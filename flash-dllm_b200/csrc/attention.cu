@@ -366,6 +366,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   static_assert(2 * (kKStages + kVStages) + 7 <= 17, "barriers below the fail flag");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kH0Bar + 18 * 8);
   volatile int32_t* fail = reinterpret_cast<volatile int32_t*>(H.bar + 17);
+  // sequence whose scores this half's scores warp found complete (-1: none);
+  // the whole CTA converts them at the end
+  volatile int32_t* convert_seq = reinterpret_cast<volatile int32_t*>(H.bar + 19);
 
   // this half's work item and key split (split = rank in the cluster)
   const int pair = blockIdx.x / p.kv_splits;
@@ -410,6 +413,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_init(pv_done, 1);
     mbar_init(mma_done, 1);
     *fail = 0;
+    *convert_seq = -1;
     fence_barrier_init();
   }
   if (warp == 8) {
@@ -721,34 +725,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
       }
       if (!__all_sync(0xffffffffu, range_ok) && lane == 0) report(p.status, FDLLM_ERR_RANGE, it.seq, kAttnKernelId);
-      // arrival: the last (item, head, split) of the sequence converts
-      const int32_t* sq = p.plan + p.plan[3] + kPlanSeq * it.seq;
+      // arrival: the last (item, head, split) of the sequence to arrive hands
+      // it to its CTA for conversion at the end
       __threadfence();
       __syncwarp();
-      int last = 0;
       if (lane == 0) {
-        const int expected = sq[1] * p.n_heads * p.kv_splits;
-        last = atomicAdd(p.score_cnt + it.seq, 1) == expected - 1;
-        if (last) p.score_cnt[it.seq] = 0;
-      }
-      if (__shfl_sync(0xffffffffu, last, 0)) {
-        __threadfence();
-        const int k_end = min(sq[2], p.seqlen_max);
-        float* dst = p.scores + static_cast<int64_t>(it.seq) * p.seqlen_max;
-        for (int n0 = 0; n0 < k_end; n0 += 32 * 4) {
-          unsigned long long v[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {  // read and zero, four in flight
-            const int n = n0 + lane + 32 * u;
-            v[u] = n < k_end ? atomicExch(acc + n, 0ull) : 0ull;
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int n = n0 + lane + 32 * u;
-            if (n < k_end)
-              dst[n] += static_cast<float>(static_cast<double>(static_cast<long long>(v[u])) * 2.3283064365386963e-10) *
-                        p.score_scale;
-          }
+        const int expected = p.plan[p.plan[3] + kPlanSeq * it.seq + 1] * p.n_heads * p.kv_splits;
+        if (atomicAdd(p.score_cnt + it.seq, 1) == expected - 1) {
+          p.score_cnt[it.seq] = 0;
+          __threadfence();
+          *convert_seq = it.seq;
         }
       }
     }
@@ -958,6 +944,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(*tmem_slot, kTcTmemCols);
+  }
+  if (!kVerify && p.scores != nullptr) {
+    // every (item, head, split) of a sequence handed here has added its
+    // column sums (each fenced before its arrival): read the accumulator row
+    // from L2, zero it, add it once to attn_scores; all threads, their loads
+    // in flight together
+#pragma unroll 1
+    for (int hh = 0; hh < 2; ++hh) {
+      const int seq = *reinterpret_cast<volatile int32_t*>(tc_half(smem, hh).bar + 19);
+      if (seq < 0) continue;  // uniform
+      const int k_end = min(p.plan[p.plan[3] + kPlanSeq * seq + 2], p.seqlen_max);
+      unsigned long long* acc = p.score_acc + static_cast<int64_t>(seq) * p.seqlen_max;
+      float* dst = p.scores + static_cast<int64_t>(seq) * p.seqlen_max;
+      for (int n0 = 0; n0 < k_end; n0 += 4 * kTcThreads) {
+        long long v[4];
+        float old[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int n = n0 + threadIdx.x + kTcThreads * u;
+          v[u] = n < k_end ? __ldcg(reinterpret_cast<const long long*>(acc + n)) : 0ll;
+          old[u] = n < k_end ? dst[n] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int n = n0 + threadIdx.x + kTcThreads * u;
+          if (n < k_end) {
+            __stcg(reinterpret_cast<long long*>(acc + n), 0ll);
+            dst[n] = old[u] + static_cast<float>(static_cast<double>(v[u]) * 2.3283064365386963e-10) * p.score_scale;
+          }
+        }
+      }
+    }
   }
 }
 

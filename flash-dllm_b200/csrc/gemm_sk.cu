@@ -124,7 +124,7 @@ __device__ __forceinline__ bool g_next(int& i, int hi, int kbt, GSeg& s) {
 // all partial loads are in flight together (one L2 latency per pair).
 // Contributors [q0, q0 + n_smem) were copied (in order) into shared memory
 // at `spart`; the others are read from the workspace.
-template <int BN>
+template <int BN, int PR>
 __device__ __forceinline__ void g_chunk2(uint32_t t_row, int ca, int cb, const GemmParams& p, int q0, int q1, int qmul,
                                          int qadd, const float4* spart, int n_smem, int r_tile, float (&va)[32],
                                          float (&vb)[32]) {
@@ -133,13 +133,13 @@ __device__ __forceinline__ void g_chunk2(uint32_t t_row, int ca, int cb, const G
   for (int q = q0; q < q1; ++q) {
     const float4* part =
         q - q0 < n_smem
-            ? spart + static_cast<size_t>(q - q0) * (kGBM * BN / 4)
-            : reinterpret_cast<const float4*>(p.partials) + static_cast<size_t>(q * qmul + qadd) * (kGBM * BN / 4);
+            ? spart + static_cast<size_t>(q - q0) * (PR * BN / 4)
+            : reinterpret_cast<const float4*>(p.partials) + static_cast<size_t>(q * qmul + qadd) * (PR * BN / 4);
     float4 xa[8], xb[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      xa[j] = part[((ca >> 2) + j) * kGBM + r_tile];
-      xb[j] = part[((cb >> 2) + j) * kGBM + r_tile];
+      xa[j] = part[((ca >> 2) + j) * PR + r_tile];
+      xb[j] = part[((cb >> 2) + j) * PR + r_tile];
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -176,10 +176,11 @@ __device__ __forceinline__ void g_prefetch_epilogue(const GemmParams& p, int row
 }
 
 // This thread's BN accumulator columns as a contributor's partial sums,
-// [col / 4][row][4] fp32, so a warp's stores are 512 contiguous bytes.
-template <int BN>
+// [col / 4][row][4] fp32 over the tile's PR valid rows, so a warp's stores
+// are 512 contiguous bytes.
+template <int BN, int PR>
 __device__ __forceinline__ void g_publish(uint32_t t_row, const GemmParams& p, int slot, int r_tile, int half) {
-  float4* part = reinterpret_cast<float4*>(p.partials) + static_cast<size_t>(slot) * (kGBM * BN / 4);
+  float4* part = reinterpret_cast<float4*>(p.partials) + static_cast<size_t>(slot) * (PR * BN / 4);
 #pragma unroll 1
   for (int c = half * 64; c < BN; c += 128) {
     float v[32], w[32];
@@ -187,8 +188,8 @@ __device__ __forceinline__ void g_publish(uint32_t t_row, const GemmParams& p, i
     tmem_ld2_32x32b_x32(t_row + c, t_row + c + 32, v, w);
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
-      __stcg(part + ((c + j) >> 2) * kGBM + r_tile, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
-      __stcg(part + ((c + 32 + j) >> 2) * kGBM + r_tile, make_float4(w[j], w[j + 1], w[j + 2], w[j + 3]));
+      __stcg(part + ((c + j) >> 2) * PR + r_tile, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+      __stcg(part + ((c + 32 + j) >> 2) * PR + r_tile, make_float4(w[j], w[j + 1], w[j + 2], w[j + 3]));
     }
   }
 }
@@ -229,7 +230,7 @@ __device__ __forceinline__ void g_stage_get8(const float4* stage, int r, int u, 
 // row0 + r), by the 8 epilogue warps (warp quarter w: rows 32 w .. 32 w + 31;
 // `half` 0 / 1 takes the even / odd column groups).  `slot` is the QKV cache
 // slot of this thread's row (-1: not written).
-template <int BN, int EPI>
+template <int BN, int EPI, int PR>
 __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_row, float4* stage, int quarter,
                                                 int half, int lane, int row0, int n_tile, int q0, int q1, int qmul,
                                                 int qadd, const float4* spart, int n_smem, int64_t slot) {
@@ -246,7 +247,7 @@ __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_
       {
         const int ch = half;
         float va[32], vb[32];
-        g_chunk2<BN>(t_row, hh * 128 + ch * 32, hh * 128 + 64 + ch * 32, p, q0, q1, qmul, qadd, spart, n_smem, r_tile,
+        g_chunk2<BN, PR>(t_row, hh * 128 + ch * 32, hh * 128 + 64 + ch * 32, p, q0, q1, qmul, qadd, spart, n_smem, r_tile,
                      va, vb);
         g_stage_put(stage, lane, va, vb);
         __syncwarp();
@@ -314,7 +315,7 @@ __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_
       const int col0 = n_tile * BN + g;
       if (col0 >= p.n_cols) break;  // uniform
       float va[32], vb[32];
-      g_chunk2<BN>(t_row, g, g + 32, p, q0, q1, qmul, qadd, spart, n_smem, r_tile, va, vb);
+      g_chunk2<BN, PR>(t_row, g, g + 32, p, q0, q1, qmul, qadd, spart, n_smem, r_tile, va, vb);
       g_stage_put(stage, lane, va, vb);
       __syncwarp();
       // 8 lanes per row: lane takes columns col0 + 8 sub .. + 7 of rows
@@ -357,7 +358,7 @@ __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_
 #pragma unroll 1
     for (int c0 = half * 32; c0 < BN / 2; c0 += 64) {
       float gv[32], uv[32];
-      g_chunk2<BN>(t_row, c0, BN / 2 + c0, p, q0, q1, qmul, qadd, spart, n_smem, r_tile, gv, uv);
+      g_chunk2<BN, PR>(t_row, c0, BN / 2 + c0, p, q0, q1, qmul, qadd, spart, n_smem, r_tile, gv, uv);
       g_stage_put(stage, lane, gv, uv);
       __syncwarp();
       const int sub = lane & 3;
@@ -389,11 +390,11 @@ __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_
 // operand ring at `ring` (idle then: a head piece is its CTA's last segment,
 // and every MMA that read the ring has completed) with bulk copies on
 // `bar`, by one thread; the epilogue then reads them from shared memory.
-template <int BN>
+template <int BN, int PR>
 __device__ __forceinline__ void g_fetch_partials(const GemmParams& p, uint8_t* ring, int q0, int n, int qmul, int qadd,
                                                  uint64_t* bar) {
-  constexpr uint32_t kSlot = kGBM * BN * 4;
-  constexpr uint32_t kPiece = 32 * 1024;
+  constexpr uint32_t kSlot = PR * BN * 4;
+  constexpr uint32_t kPiece = kSlot < 32 * 1024 ? kSlot : 32 * 1024;
   mbar_arrive_expect_tx(bar, static_cast<uint32_t>(n) * kSlot);
   for (int j = 0; j < n; ++j) {
     const uint8_t* src = reinterpret_cast<const uint8_t*>(p.partials) + static_cast<size_t>((q0 + j) * qmul + qadd) * kSlot;
@@ -485,7 +486,32 @@ __global__ void __launch_bounds__(kGThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // A comes from the kernel before (programmatic launch)
+  constexpr uint32_t kTx = static_cast<uint32_t>(C::kStageBytes);
+  // B (weights: never written by the kernel before) of the stages that need
+  // no free slot, requested before the programmatic-launch wait so its
+  // latency overlaps the tail of the kernel before; A comes from that kernel
+  auto load_b = [&](int n_tile, int kb, int s) {
+    int b_row = 0;
+    const CUtensorMap* map_b = g_b_coord<EPI>(p, n_tile, BN, 0, BN, &map_b0, &map_b1, &map_b2, b_row);
+    uint8_t* b0 = smem + s * C::kStageBytes + C::kABytes;
+#pragma unroll
+    for (int sub = 0; sub < KSUB; ++sub) {
+      const int kx = (kb * KSUB + sub) * kGBK;
+      uint8_t* b = b0 + sub * C::kBSub;
+      tma_load_2d(b, map_b, kx, b_row, &full[s]);
+      if (EPI == kEpiSwiglu) tma_load_2d(b + (BN / 2) * 128, map_b, kx, p.hidden + b_row, &full[s]);
+    }
+  };
+  uint32_t n_pre = 0;
+  if (warp == 0 && lane == 0) {
+    int i = lo;
+    GSeg sg;
+    while (n_pre < static_cast<uint32_t>(C::kStages) && g_next(i, hi, p.kbt, sg))
+      for (int kb = sg.k0; kb < sg.k1 && n_pre < static_cast<uint32_t>(C::kStages); ++kb, ++n_pre) {
+        mbar_arrive_expect_tx(&full[n_pre], kTx);
+        load_b(sg.tile / m_tiles_in, kb, static_cast<int>(n_pre));
+      }
+  }
   pdl_wait();
   pdl_launch_dependents();
 
@@ -494,37 +520,26 @@ __global__ void __launch_bounds__(kGThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer --
     if (lane == 0) {
-      constexpr uint32_t kTx = static_cast<uint32_t>(C::kStageBytes);
       uint32_t g = 0;
       bool ok = true;
       int i = lo;
       GSeg sg;
       while (ok && g_next(i, hi, p.kbt, sg)) {
         const int m_tile = p.groups > 1 ? group : sg.tile % m_tiles_in, n_tile = sg.tile / m_tiles_in;
-        int b_row = 0;
-        const CUtensorMap* map_b = g_b_coord<EPI>(p, n_tile, BN, 0, BN, &map_b0, &map_b1, &map_b2, b_row);
         for (int kb = sg.k0; kb < sg.k1; ++kb, ++g) {
           const int s = g % C::kStages;
           const uint32_t ph = (g / C::kStages) & 1;
+          const bool pre = g < n_pre;  // B already requested, tx already expected
           if (g >= static_cast<uint32_t>(C::kStages) && !mbar_wait(&empty[s], ph ^ 1, p.status, kGemmKernelId)) {
             ok = false;
             break;
           }
           uint8_t* a0 = smem + s * C::kStageBytes;
-          uint8_t* b0 = a0 + C::kABytes;
-          mbar_arrive_expect_tx(&full[s], kTx);
+          if (!pre) mbar_arrive_expect_tx(&full[s], kTx);
 #pragma unroll
-          for (int sub = 0; sub < KSUB; ++sub) {
-            const int kx = (kb * KSUB + sub) * kGBK;
-            tma_load_2d(a0 + sub * C::kASub, &map_a, kx, m_tile * kGBM, &full[s]);
-            uint8_t* b = b0 + sub * C::kBSub;
-            if (EPI == kEpiSwiglu) {
-              tma_load_2d(b, map_b, kx, b_row, &full[s]);
-              tma_load_2d(b + (BN / 2) * 128, map_b, kx, p.hidden + b_row, &full[s]);
-            } else {
-              tma_load_2d(b, map_b, kx, b_row, &full[s]);
-            }
-          }
+          for (int sub = 0; sub < KSUB; ++sub)
+            tma_load_2d(a0 + sub * C::kASub, &map_a, (kb * KSUB + sub) * kGBK, m_tile * kGBM, &full[s]);
+          if (!pre) load_b(n_tile, kb, s);
         }
       }
     }
@@ -593,14 +608,19 @@ __global__ void __launch_bounds__(kGThreads, 1)
       if (*abort_flag != 0) break;
       tc_fence_after();
       if (sg.k0 > 0) {
-        // tail piece (this CTA's first segment): publish the partial sums
-        g_publish<BN>(t_row, p, cta, r_tile, half);
+        // tail piece (this CTA's first segment): publish the partial sums of
+        // the tile's XROWS valid rows; after the barrier one thread's release
+        // (cumulative over the CTA's stores ordered by the barrier) raises
+        // the flag
+        if (quarter * 32 < XROWS) g_publish<BN, XROWS>(t_row, p, cta, r_tile, half);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        __threadfence();
         asm volatile("bar.sync 1, 256;" ::: "memory");
-        if (ep_tid == 0) st_release_gpu(p.flags + cta, 1);
+        if (ep_tid == 0) {
+          __threadfence();
+          st_release_gpu(p.flags + cta, 1);
+        }
         ++seg;
         continue;
       }
@@ -619,12 +639,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
       }
       int n_smem = 0;
       if (q_end > cta + 1) {
-        n_smem = min(q_end - cta - 1, C::kBarOffset / (kGBM * BN * 4));
-        if (ep_tid == 0) g_fetch_partials<BN>(p, smem, cta + 1, n_smem, 1, 0, fix_bar);
+        n_smem = min(q_end - cta - 1, C::kBarOffset / (XROWS * BN * 4));
+        if (ep_tid == 0) g_fetch_partials<BN, XROWS>(p, smem, cta + 1, n_smem, 1, 0, fix_bar);
         if (!mbar_wait(fix_bar, 0, p.status, kGemmKernelId)) n_smem = 0;  // (recorded; sums then incomplete)
       }
-      g_tile_epilogue<BN, EPI>(p, t_row, stage, quarter, half, lane, row0, n_tile, cta + 1, q_end, 1, 0,
-                               reinterpret_cast<const float4*>(smem), n_smem, slot);
+      if (quarter * 32 < XROWS)  // accumulator rows past XROWS hold no data
+        g_tile_epilogue<BN, EPI, XROWS>(p, t_row, stage, quarter, half, lane, row0, n_tile, cta + 1, q_end, 1, 0,
+                                        reinterpret_cast<const float4*>(smem), n_smem, slot);
       // every column of this accumulator has been read
       tc_fence_before();
       __syncwarp();
@@ -728,6 +749,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
   cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // B (weights) of the stages that need no free slot, requested before the
+  // programmatic-launch wait (see the single-CTA kernel); A after it
+  auto load_b = [&](int n_tile, int kb, int s) {
+    int b_row = 0;
+    const CUtensorMap* map_b =
+        g_b_coord<EPI>(p, n_tile, BN, static_cast<int>(rank), kGBM, &map_b0, &map_b1, &map_b2, b_row);
+    const uint32_t bar = mapa_shared(&full[s], 0);
+#pragma unroll
+    for (int sub = 0; sub < KSUB; ++sub)
+      tma_load_2d_pair(smem + s * C::kStageBytes + C::kABytes + sub * C::kSub, map_b, (kb * KSUB + sub) * kGBK, b_row,
+                       bar);
+  };
+  uint32_t n_pre = 0;
+  if (warp == 0 && lane == 0) {
+    int i = lo;
+    GSeg sg;
+    while (n_pre < static_cast<uint32_t>(C::kStages) && g_next(i, hi, p.kbt, sg))
+      for (int kb = sg.k0; kb < sg.k1 && n_pre < static_cast<uint32_t>(C::kStages); ++kb, ++n_pre) {
+        if (rank == 0) mbar_arrive_expect_tx(&full[n_pre], 2u * C::kStageBytes);
+        load_b(sg.tile / m_tiles_in, kb, static_cast<int>(n_pre));
+      }
+  }
   pdl_wait();
   pdl_launch_dependents();
 
@@ -743,25 +786,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
       while (ok && g_next(i, hi, p.kbt, sg)) {
         const int m_tile = p.groups > 1 ? group : sg.tile % m_tiles_in, n_tile = sg.tile / m_tiles_in;
         const int a_row = m_tile * 2 * kGBM + static_cast<int>(rank) * kGBM;
-        int b_row = 0;
-        const CUtensorMap* map_b =
-            g_b_coord<EPI>(p, n_tile, BN, static_cast<int>(rank), kGBM, &map_b0, &map_b1, &map_b2, b_row);
         for (int kb = sg.k0; kb < sg.k1; ++kb, ++g) {
           const int s = g % C::kStages;
           const uint32_t ph = (g / C::kStages) & 1;
+          const bool pre = g < n_pre;  // B already requested, tx already expected
           if (g >= static_cast<uint32_t>(C::kStages) && !mbar_wait(&empty[s], ph ^ 1, p.status, kGemmKernelId)) {
             ok = false;
             break;
           }
           uint8_t* a0 = smem + s * C::kStageBytes;
           const uint32_t bar = mapa_shared(&full[s], 0);
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2u * C::kStageBytes);
+          if (rank == 0 && !pre) mbar_arrive_expect_tx(&full[s], 2u * C::kStageBytes);
 #pragma unroll
-          for (int sub = 0; sub < KSUB; ++sub) {
-            const int kx = (kb * KSUB + sub) * kGBK;
-            tma_load_2d_pair(a0 + sub * C::kSub, &map_a, kx, a_row, bar);
-            tma_load_2d_pair(a0 + C::kABytes + sub * C::kSub, map_b, kx, b_row, bar);
-          }
+          for (int sub = 0; sub < KSUB; ++sub)
+            tma_load_2d_pair(a0 + sub * C::kSub, &map_a, (kb * KSUB + sub) * kGBK, a_row, bar);
+          if (!pre) load_b(n_tile, kb, s);
         }
       }
     }
@@ -830,13 +869,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
       if (*abort_flag != 0) break;
       tc_fence_after();
       if (sg.k0 > 0) {
-        g_publish<BN>(t_row, p, cta, r_tile, half);
+        g_publish<BN, kGBM>(t_row, p, cta, r_tile, half);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(acc_empty_leader[acc]);
-        __threadfence();
         asm volatile("bar.sync 1, 256;" ::: "memory");
-        if (ep_tid == 0) st_release_gpu(p.flags + cta, 1);
+        if (ep_tid == 0) {
+          __threadfence();
+          st_release_gpu(p.flags + cta, 1);
+        }
         ++seg;
         continue;
       }
@@ -856,10 +897,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
       int n_smem = 0;
       if (q_end > pair + 1) {
         n_smem = min(q_end - pair - 1, C::kBarOffset / (kGBM * BN * 4));
-        if (ep_tid == 0) g_fetch_partials<BN>(p, smem, pair + 1, n_smem, 2, static_cast<int>(rank), fix_bar);
+        if (ep_tid == 0) g_fetch_partials<BN, kGBM>(p, smem, pair + 1, n_smem, 2, static_cast<int>(rank), fix_bar);
         if (!mbar_wait(fix_bar, 0, p.status, kGemmKernelId)) n_smem = 0;  // (recorded; sums then incomplete)
       }
-      g_tile_epilogue<BN, EPI>(p, t_row, stage, quarter, half, lane, row0, n_tile, pair + 1, q_end, 2,
+      g_tile_epilogue<BN, EPI, kGBM>(p, t_row, stage, quarter, half, lane, row0, n_tile, pair + 1, q_end, 2,
                                static_cast<int>(rank), reinterpret_cast<const float4*>(smem), n_smem, slot);
       tc_fence_before();
       __syncwarp();
