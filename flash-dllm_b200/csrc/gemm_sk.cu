@@ -610,17 +610,14 @@ __global__ void __launch_bounds__(kGThreads, 1)
       if (sg.k0 > 0) {
         // tail piece (this CTA's first segment): publish the partial sums of
         // the tile's XROWS valid rows; after the barrier one thread's release
-        // (cumulative over the CTA's stores ordered by the barrier) raises
-        // the flag
+        // store (cumulative over the CTA's stores ordered by the barrier)
+        // raises the flag
         if (quarter * 32 < XROWS) g_publish<BN, XROWS>(t_row, p, cta, r_tile, half);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
         asm volatile("bar.sync 1, 256;" ::: "memory");
-        if (ep_tid == 0) {
-          __threadfence();
-          st_release_gpu(p.flags + cta, 1);
-        }
+        if (ep_tid == 0) st_release_gpu(p.flags + cta, 1);
         ++seg;
         continue;
       }
@@ -874,10 +871,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(acc_empty_leader[acc]);
         asm volatile("bar.sync 1, 256;" ::: "memory");
-        if (ep_tid == 0) {
-          __threadfence();
-          st_release_gpu(p.flags + cta, 1);
-        }
+        if (ep_tid == 0) st_release_gpu(p.flags + cta, 1);
         ++seg;
         continue;
       }
