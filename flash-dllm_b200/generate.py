@@ -65,14 +65,20 @@ def _tiles(rows: List, j: int, k_end: int, start: int, n: int, bm: int) -> None:
 
 class _Forwarder:
     """Runs the model's forward passes.  A forward whose input shapes were
-    seen before is captured into a CUDA graph (on its second occurrence, after
+    seen before is captured into CUDA graphs (on its second occurrence, after
     an eager run of that same step sized the workspaces) and replayed from
     then on, with the step's inputs copied into the graph's static tensors.
     Forwards are pure functions of their inputs apart from the in-place cache
-    and score updates, which the graph performs exactly like the eager call."""
+    and score updates, which the graph performs exactly like the eager call.
 
-    def __init__(self, enabled: bool):
+    A forward is captured as two graphs, split after layer ``split_after``:
+    launching a graph of a few hundred kernels takes the host ~0.3 ms, during
+    which the GPU would wait; the small first graph starts the GPU at once and
+    the large second one is launched while it runs."""
+
+    def __init__(self, enabled: bool, split_after: int = 2):
         self.enabled = enabled
+        self.split_after = split_after
         self.seen = {}
         self.graphs = {}
         self.pool = None
@@ -80,37 +86,75 @@ class _Forwarder:
 
     def __call__(self, key, inputs: dict, build):
         if not self.enabled:
-            return build(inputs)
+            return build(inputs, None)
         hit = self.graphs.get(key)
         if hit is not None:
-            static, graph, out = hit
+            static, graphs, out = hit
             for name, t in inputs.items():
                 static[name].copy_(t)
-            graph.replay()
+            for graph in graphs:
+                graph.replay()
             return out
         self.seen[key] = self.seen.get(key, 0) + 1
         if self.seen[key] < 2:
-            return build(inputs)
+            return build(inputs, None)
         static = {name: t.clone() for name, t in inputs.items()}
-        result = build(static)  # this step's real forward; also sizes workspaces
+        result = build(static, None)  # this step's real forward; also sizes workspaces
         # Capture on a side stream into one memory pool shared by all of this
         # generation's graphs.  (torch.cuda.graph would also run gc and empty
         # the allocator cache before every capture: ~0.5 s each.)
         if self.pool is None:
             self.pool = torch.cuda.graph_pool_handle()
             self.stream = torch.cuda.Stream()
-        graph = torch.cuda.CUDAGraph()
+        graphs = [torch.cuda.CUDAGraph()]
+
+        def split(block_idx: int) -> None:
+            if block_idx == self.split_after:
+                graphs[-1].capture_end()
+                graphs.append(torch.cuda.CUDAGraph())
+                graphs[-1].capture_begin(pool=self.pool)
+
         cur = torch.cuda.current_stream()
         self.stream.wait_stream(cur)
         with torch.cuda.stream(self.stream):
-            graph.capture_begin(pool=self.pool)
+            graphs[0].capture_begin(pool=self.pool)
             try:
-                out = build(static)
+                out = build(static, split)
             finally:
-                graph.capture_end()
+                graphs[-1].capture_end()
         cur.wait_stream(self.stream)
-        self.graphs[key] = (static, graph, out)
+        self.graphs[key] = (static, graphs, out)
         return result
+
+
+class _Staging:
+    """Pinned host buffers for the host->device copies of a step's tables,
+    reused across steps (pinning a fresh host tensor per copy costs a few
+    hundred microseconds of host time while the GPU waits).  A ring of
+    buffers; one is refilled only after the copy that last read it is done."""
+
+    def __init__(self, n: int = 4):
+        self.bufs = [None] * n
+        self.events = [None] * n
+        self.i = 0
+
+    def send(self, t: torch.Tensor, dev) -> torch.Tensor:
+        k = self.i
+        self.i = (self.i + 1) % len(self.bufs)
+        nbytes = t.numel() * t.element_size()
+        if self.events[k] is not None:
+            self.events[k].synchronize()
+        buf = self.bufs[k]
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8).pin_memory()
+            self.bufs[k] = buf
+        staged = buf[:nbytes].view(t.dtype).view(t.shape)
+        staged.copy_(t)
+        out = staged.to(dev, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self.events[k] = ev
+        return out
 
 
 class _Session:
@@ -132,6 +176,7 @@ class _Session:
         self.empty_i32 = torch.zeros(0, device=dev, dtype=torch.int32)
         self.empty_i64 = torch.zeros(0, device=dev, dtype=torch.int64)
         self.forward = _Forwarder(use_graphs and dev.type == "cuda")
+        self.staging = _Staging() if dev.type == "cuda" else None
 
     def reset(self, model) -> None:
         for block, (kc, vc) in zip(model.model.transformer.blocks, self.caches):
@@ -241,7 +286,10 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
 
     def h2d(t: torch.Tensor) -> torch.Tensor:
         io["h2d_bytes"] += t.numel() * t.element_size()
-        return t.pin_memory().to(dev, non_blocking=True) if t.device.type == "cpu" else t
+        if t.device.type != "cpu":
+            return t
+        staging = sess.staging
+        return staging.send(t.contiguous(), dev) if staging is not None else t.to(dev)
 
     def d2h(t: torch.Tensor) -> list:
         io["d2h_bytes"] += t.numel() * t.element_size()
@@ -334,14 +382,13 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         x_query = x[query_pos_flat]
         n_m = len(m_rows)
 
-        def cache_forward(t, n_m=n_m, r_m=r_m, has_t=bool(t_rows)):
+        def cache_forward(t, hook, n_m=n_m, r_m=r_m, has_t=bool(t_rows)):
             masked_blocks = t["tables"][:n_m] if n_m else empty_i32
             tracked_blocks = t["tables"][n_m:] if has_t else empty_i32
             positions = [t["qpos"], empty_i64, rotary_emb_pos, [], attn_scores, []]
             lengths = [start_layer, None, masked_blocks, tracked_blocks, t["tables"], st.active, n_m, L, bm, bn,
                        None, False]
-            return model(t["x"].unsqueeze(0), use_cache=True, lengths=lengths, positions=positions,
-                         logit_rows=r_m).logits[0]
+            return _call_model(model, t["x"].unsqueeze(0), lengths, positions, r_m, hook)
 
         logits = forward(("cache", x_query.numel(), n_m, len(t_rows), r_m),
                          {"x": x_query, "qpos": query_pos_flat, "tables": tables}, cache_forward)
@@ -405,11 +452,10 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
             info2_d = info2_d.view(-1, 4)
             eos_known = eos_known.to(torch.int32)
 
-            def verify_forward(t, n_m=n_m):
+            def verify_forward(t, hook, n_m=n_m):
                 positions = [t["qpos"], t["kpos"], rotary_emb_pos, [], attn_scores, t["mask"]]
                 lengths = [start_layer, t["vblocks"], None, empty_i32, None, st.active, n_m, L, bm, bn, None, True]
-                return model(t["x"].unsqueeze(0), use_cache=True, lengths=lengths, positions=positions,
-                             logit_rows=t["lidx"]).logits[0]
+                return _call_model(model, t["x"].unsqueeze(0), lengths, positions, t["lidx"], hook)
 
             if sum(s_list) > 0:
                 logits_v = forward(("verify", x_verify.numel(), key_pos_flat.numel(), len(vrows), lidx.numel()),
@@ -494,6 +540,13 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         if max_steps is not None and step >= max_steps:
             break
     return responses, num_tokens, max_num_tokens
+
+
+def _call_model(model, x, lengths, positions, logit_rows, hook):
+    """The model's forward; ``hook`` (a graph-capture split) only reaches
+    models whose forward takes ``layer_hook`` (this package's)."""
+    kw = {"layer_hook": hook} if hook is not None else {}
+    return model(x, use_cache=True, lengths=lengths, positions=positions, logit_rows=logit_rows, **kw).logits[0]
 
 
 def _continues(full_pos, ar_L, act_d, nd_d, keep_d, pred_d, eos_known, eos_d) -> torch.Tensor:

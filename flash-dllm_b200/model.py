@@ -139,14 +139,17 @@ class LLaDAModelB200(nn.Module):
 
     @torch.no_grad()
     def forward(self, input_ids: torch.Tensor, use_cache: bool = True, lengths=None, positions=None,
-                logit_rows: Optional[torch.Tensor] = None, **_unused):
+                logit_rows: Optional[torch.Tensor] = None, layer_hook=None, **_unused):
         """``input_ids`` (1, Nq) -> ``.logits`` (1, Nq, vocab), or (1, R, vocab)
         for the R rows listed in ``logit_rows`` (an int64 index tensor or an
-        int prefix length)."""
+        int prefix length).  ``layer_hook(block_idx)`` runs after each block
+        (the decode loop uses it to split a CUDA-graph capture)."""
         t = self.model.transformer
         x = t.wte(input_ids.reshape(-1))
         for block_idx, block in enumerate(t.blocks):
             x = flash_fused_elastic_cache(block, x, block_idx, positions, lengths).squeeze(0)
+            if layer_hook is not None:
+                layer_hook(block_idx)
         if logit_rows is not None:
             x = x[:logit_rows] if isinstance(logit_rows, int) else x.index_select(0, logit_rows)
         x = t.ln_f(x.contiguous())
