@@ -890,12 +890,13 @@ QkvOverride& qkv_override() {
   return o;
 }
 
-// Kernel choice: the stream-K GEMM above 128 rows (512 rows: 51.7 vs 57.7
-// us), the whole-tile kernel up to 128 (64 rows: 27.2 vs 30.1 us), unless
+// Kernel choice: the stream-K GEMM at every row count (back to back with the
+// weights streaming from HBM: 64 rows 24.9 vs 25.2 us, 128 rows 28.0 vs
+// 30.6 us, 512 rows 55 vs 58 us against the whole-tile kernels), unless
 // overridden.
 bool qkv_use_sk(int32_t n_rows) {
-  const int impl = qkv_override().impl;
-  return impl == 0 || (impl < 0 && n_rows > 128);
+  (void)n_rows;
+  return qkv_override().impl != 1;
 }
 
 // Units are spread round-robin over one CTA per SM.  Tiles are 128 columns

@@ -73,7 +73,7 @@ int fdllm_swiglu(const void* gate, const void* up, void* out, int64_t rows, int3
                  cudaStream_t stream);
 
 /* Override the QKV kernel's plan (tuning and tests; not thread-safe against concurrent calls).
- * impl -1 = automatic (the stream-K GEMM above 128 rows), 0 = the stream-K GEMM (tile width and ring
+ * impl -1 = automatic (the stream-K GEMM at every row count), 0 = the stream-K GEMM (tile width and ring
  * from fdllm_gemm_set_plan), 1 = the earlier whole-tile kernels, where bn = tile width 64 or 128 columns (0: automatic), splits = K splits
  * (0 or 1: none), ksub = 64-wide K sub-tiles per ring slot 1 or 2 (0: automatic), pair = CTA-pair
  * kernel above 128 rows: 1 on, 0 off, -1 automatic.  The initial values come from the
