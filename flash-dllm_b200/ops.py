@@ -128,11 +128,20 @@ def _check(t: torch.Tensor, name: str, dtype=None, dim=None) -> None:
         raise ValueError(f"{name} must be contiguous")
 
 
-def _stream() -> int:
-    # torch's current stream on the current device (the capture stream while
-    # a CUDA graph is being captured); the raw lookup avoids the ~15 us of
-    # Python in torch.cuda.current_stream() per kernel call
+def _stream_public() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _stream_raw() -> int:
     return torch._C._cuda_getCurrentRawStream(torch._C._cuda_getDevice())
+
+
+# torch's current stream on the current device (the capture stream while a
+# CUDA graph is being captured).  The raw lookup avoids ~15 us of Python in
+# torch.cuda.current_stream() per kernel call; a torch without it gets the
+# public call.
+_stream = _stream_raw if hasattr(torch._C, "_cuda_getCurrentRawStream") and hasattr(torch._C, "_cuda_getDevice") \
+    else _stream_public
 
 
 @functools.lru_cache(maxsize=None)
