@@ -31,6 +31,26 @@ constexpr int kRefreshMax = 8192;
 __device__ __forceinline__ float bf16_to_f(__nv_bfloat16 h) { return __bfloat162float(h); }
 
 // ------------------------------------------------------------ row stats ----
+// exp of every bf16 value in fp64, indexed by the bf16 bit pattern: for
+// |x|, |m| <= 512, exp(x - m) = exp(x) * exp(-m), two correctly rounded
+// factors and one rounded product (<= ~1.5 ulp, the order of the fp64
+// summation's own rounding), one L1-resident load and one multiply instead of
+// an fp64 exp per logit (the row pass was bound by fp64 exp throughput).
+// Larger magnitudes take the fp64 exp.
+__device__ double g_exp_bf16[65536];
+
+__global__ void exp_table_kernel() {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < 65536) {
+    const __nv_bfloat16 h = __ushort_as_bfloat16(static_cast<unsigned short>(i));
+    const float x = __bfloat162float(h);
+    g_exp_bf16[i] = fabsf(x) <= 512.f ? exp(static_cast<double>(x)) : 0.0;
+  }
+}
+
+// |x| <= 512 for a bf16 bit pattern: exponent field below 2^9, finite
+__device__ __forceinline__ bool small_bf16(unsigned short bits) { return (bits & 0x7f80u) < 0x4400u; }
+
 __global__ void __launch_bounds__(kStatsThreads) row_stats_kernel(const __nv_bfloat16* __restrict__ logits,
                                                                   int64_t ld, int vocab,
                                                                   const int64_t* __restrict__ tokens,
@@ -42,11 +62,34 @@ __global__ void __launch_bounds__(kStatsThreads) row_stats_kernel(const __nv_bfl
   __shared__ float s_max[kStatsThreads / 32];
   __shared__ int s_idx[kStatsThreads / 32];
   __shared__ double s_sum[kStatsThreads / 32];
+  // 16-byte loads of 8 logits when the row allows it (the vocabulary and the
+  // row stride multiples of 8, an aligned base), single logits for the rest
+  const bool vec = (ld % 8 == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
+  const int nvec = vec ? vocab / 8 : 0;
+  const uint4* rowv = reinterpret_cast<const uint4*>(row);
   float m = -INFINITY;
   int mi = INT32_MAX;
-  for (int i = threadIdx.x; i < vocab; i += kStatsThreads) {
+  // strictly greater: the first index wins within a thread (its indices increase)
+#pragma unroll 4
+  for (int i = threadIdx.x; i < nvec; i += kStatsThreads) {
+    const uint4 u = __ldg(rowv + i);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      if (f.x > m) {
+        m = f.x;
+        mi = 8 * i + 2 * e;
+      }
+      if (f.y > m) {
+        m = f.y;
+        mi = 8 * i + 2 * e + 1;
+      }
+    }
+  }
+  for (int i = 8 * nvec + threadIdx.x; i < vocab; i += kStatsThreads) {
     const float v = bf16_to_f(row[i]);
-    if (v > m) {  // strictly greater: first index wins within a thread (indices increase)
+    if (v > m) {
       m = v;
       mi = i;
     }
@@ -86,7 +129,21 @@ __global__ void __launch_bounds__(kStatsThreads) row_stats_kernel(const __nv_bfl
   __syncthreads();
   const double md = static_cast<double>(s_max[0]);
   double sum = 0.0;
-  for (int i = threadIdx.x; i < vocab; i += kStatsThreads) sum += exp(static_cast<double>(bf16_to_f(row[i])) - md);
+  const bool table = fabsf(s_max[0]) <= 512.f;
+  const double em = table ? exp(-md) : 0.0;
+#pragma unroll 2
+  for (int i = threadIdx.x; i < nvec; i += kStatsThreads) {
+    const uint4 u = __ldg(rowv + i);
+    const unsigned short* b = reinterpret_cast<const unsigned short*>(&u);
+    double part = 0.0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      part += (table && small_bf16(b[e])) ? __ldg(g_exp_bf16 + b[e]) * em
+                                          : exp(static_cast<double>(bf16_to_f(__ushort_as_bfloat16(b[e]))) - md);
+    }
+    sum += part;
+  }
+  for (int i = 8 * nvec + threadIdx.x; i < vocab; i += kStatsThreads) sum += exp(static_cast<double>(bf16_to_f(row[i])) - md);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (l == 0) s_sum[w] = sum;
@@ -332,6 +389,14 @@ int fdllm_row_stats(const void* logits, int64_t ld, int32_t n_rows, int32_t voca
       (p_tok != nullptr && tokens == nullptr))
     return FDLLM_ERR_ARG;
   if (n_rows == 0) return FDLLM_OK;
+  static bool table_ready[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FDLLM_ERR_CUDA;
+  if (!table_ready[dev]) {  // stream-ordered before the first row pass on this device
+    fdllm::exp_table_kernel<<<256, 256, 0, stream>>>();
+    if (cudaPeekAtLastError() != cudaSuccess) return FDLLM_ERR_CUDA;
+    table_ready[dev] = true;
+  }
   fdllm::row_stats_kernel<<<n_rows, fdllm::kStatsThreads, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(logits), ld, vocab, tokens, p_max, argmax, p_tok);
   return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;

@@ -28,6 +28,35 @@ def test_row_stats_matches_fp64_softmax_with_ties():
     assert torch.allclose(pt.cpu(), pto, rtol=1e-12, atol=1e-300)
 
 
+@pytest.mark.parametrize("vocab,pad,scale,shift", [
+    (126464, 0, 3.0, 0.0),      # 16-byte loads, every logit through the bf16 exp table
+    (1000, 0, 3.0, 0.0),        # vocabulary a multiple of 8, small
+    (1001, 7, 3.0, 0.0),        # odd vocabulary and padded row stride: single-logit loads
+    (4096, 0, 300.0, 0.0),      # maximum beyond 512: fp64 exp path for the whole row
+    (4096, 0, 3.0, 600.0),      # ... at a large offset
+    (4096, 0, -1.0, 0.0),       # table for most logits, fp64 exp for outliers at -700 and -inf
+])
+def test_row_stats_load_paths(vocab, pad, scale, shift):
+    """Every load / exponential path of the row pass against the fp64
+    softmax: vectorised and single-logit loads, the bf16 exp table and the
+    fp64 exp for magnitudes above 512."""
+    import flash_dllm_b200.ops as ops
+    g = torch.Generator().manual_seed(vocab + pad)
+    R = 19
+    full = (torch.randn(R, vocab + pad, generator=g) * abs(scale) + shift).bfloat16()
+    if scale < 0:
+        full[:, ::97] = -700.0
+        full[:, 5::211] = float("-inf")
+    logits = full[:, :vocab]
+    tok = torch.randint(0, vocab, (R,), generator=g)
+    p, am, pt = ops.row_stats(full.cuda()[:, :vocab], tok.cuda())
+    po, amo = do.confidence(logits.contiguous())
+    pto = do.token_prob(logits.contiguous(), tok)
+    assert torch.equal(am.cpu(), amo)
+    assert torch.allclose(p.cpu(), po, rtol=1e-12, atol=0)
+    assert torch.allclose(pt.cpu(), pto, rtol=1e-12, atol=1e-300)
+
+
 def _accept_case(seed, B, bm, L):
     rs = np.random.RandomState(seed)
     rows, info, window, eos_known, lens = [], [], [], [], []
