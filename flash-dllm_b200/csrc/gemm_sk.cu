@@ -179,13 +179,15 @@ __device__ __forceinline__ void g_prefetch_epilogue(const GemmParams& p, int row
 // [col / 4][row][4] fp32 over the tile's PR valid rows, so a warp's stores
 // are 512 contiguous bytes.
 template <int BN, int PR>
-__device__ __forceinline__ void g_publish(uint32_t t_row, const GemmParams& p, int slot, int r_tile, int half) {
+__device__ __forceinline__ void g_publish(uint32_t t_row, const GemmParams& p, int slot, int r_tile, int half,
+                                          bool valid) {
   float4* part = reinterpret_cast<float4*>(p.partials) + static_cast<size_t>(slot) * (PR * BN / 4);
 #pragma unroll 1
   for (int c = half * 64; c < BN; c += 128) {
     float v[32], w[32];
     __syncwarp();
-    tmem_ld2_32x32b_x32(t_row + c, t_row + c + 32, v, w);
+    tmem_ld2_32x32b_x32(t_row + c, t_row + c + 32, v, w);  // all lanes (warp-wide)
+    if (!valid) continue;
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
       __stcg(part + ((c + j) >> 2) * PR + r_tile, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
@@ -226,16 +228,19 @@ __device__ __forceinline__ void g_stage_get8(const float4* stage, int r, int u, 
   v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
 }
 
-// Epilogue of one tile on this CTA's 128 accumulator rows (global rows
-// row0 + r), by the 8 epilogue warps (warp quarter w: rows 32 w .. 32 w + 31;
-// `half` 0 / 1 takes the even / odd column groups).  `slot` is the QKV cache
-// slot of this thread's row (-1: not written).
-template <int BN, int EPI, int PR>
+// Epilogue of one tile on this CTA's accumulator rows (global rows row0 +
+// r), by the 8 epilogue warps: warp quarter w holds rows RQ w .. RQ w + RQ - 1
+// in its TMEM lanes 0 .. RQ - 1 (RQ = 32 for M = 128 accumulators, 16 for
+// M = 64, whose rows sit in the first 16 lanes of each lane quarter);
+// `half` 0 / 1 takes the even / odd column groups.  `slot` is the QKV cache
+// slot of this thread's row (-1: not written).  Lanes past RQ read row 0 of
+// their quarter's partials and write nothing.
+template <int BN, int EPI, int PR, int RQ>
 __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_row, float4* stage, int quarter,
                                                 int half, int lane, int row0, int n_tile, int q0, int q1, int qmul,
                                                 int qadd, const float4* spart, int n_smem, int64_t slot) {
-  const int r_tile = quarter * 32 + lane;
-  const int wrow0 = row0 + quarter * 32;  // global row of the warp's staged row 0
+  const int r_tile = quarter * RQ + (lane < RQ ? lane : 0);
+  const int wrow0 = row0 + quarter * RQ;  // global row of the warp's staged row 0
   if (EPI == kEpiQkv) {
 #pragma unroll 1
     for (int hh = 0; hh < BN / 128; ++hh) {
@@ -257,7 +262,7 @@ __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_
         const int sub = lane & 3;
         const int c = ch * 32 + 8 * sub;
 #pragma unroll 1
-        for (int it = 0; it < 4; it += 2) {
+        for (int it = 0; it < RQ / 8; it += 2) {
           int64_t sl[2];
           float4 tb[2][8];
 #pragma unroll
@@ -326,7 +331,7 @@ __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_
       uint4 rv[8];
       if (p.res != nullptr) {
 #pragma unroll
-        for (int it = 0; it < 8; ++it) {
+        for (int it = 0; it < RQ / 4; ++it) {
           const int row = wrow0 + it * 4 + (lane >> 3);
           rv[it] = (row < p.n_rows && col < p.n_cols)
                        ? __ldg(reinterpret_cast<const uint4*>(p.res + static_cast<int64_t>(row) * p.ld_res + col))
@@ -334,7 +339,7 @@ __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_
         }
       }
 #pragma unroll
-      for (int it = 0; it < 8; ++it) {
+      for (int it = 0; it < RQ / 4; ++it) {
         const int rr = it * 4 + (lane >> 3);
         const int row = wrow0 + rr;
         float v[8];
@@ -364,7 +369,7 @@ __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_
       const int sub = lane & 3;
       const int col = n_tile * (BN / 2) + c0 + 8 * sub;
 #pragma unroll 1
-      for (int it = 0; it < 4; ++it) {
+      for (int it = 0; it < RQ / 8; ++it) {
         const int rr = it * 8 + (lane >> 2);
         const int row = wrow0 + rr;
         float g8[8], u8[8];
@@ -546,7 +551,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
   } else if (warp == 1) {
     // -------------------------------------------------------- MMA issuer --
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kGBM, BN);
+      // M = 64 UMMAs for 64-row A tiles (no idle accumulator rows)
+      constexpr uint32_t idesc = umma_idesc_bf16(XROWS == 64 ? 64 : kGBM, BN);
       uint32_t g = 0;
       int seg = 0;
       bool ok = true;
@@ -585,9 +591,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kGRegsHigh));
     // ---------------------------------------------------------- epilogue --
+    // accumulator rows per TMEM lane quarter: 32 (M = 128) or 16 (M = 64,
+    // lanes 0-15 of each quarter)
+    constexpr int kRQ = XROWS == 64 ? 16 : 32;
     const int quarter = warp & 3;
     const int half = (warp - 4) >> 2;
-    const int r_tile = quarter * 32 + lane;
+    const bool row_lane = lane < kRQ;
+    const int r_tile = quarter * kRQ + (row_lane ? lane : 0);
     const int ep_tid = threadIdx.x - 128;
     float4* stage = stage_all + (warp - 4) * (32 * 16);
     int seg = 0;
@@ -599,8 +609,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
       const int row0 = m_tile * kGBM;
       const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
       // the QKV epilogue's slot, fetched while the MMAs run
-      const int64_t slot = (EPI == kEpiQkv && sg.k0 == 0) ? g_qkv_slot(p, row0 + r_tile) : -1;
-      if (sg.k0 == 0 && half == 0) g_prefetch_epilogue<BN, EPI>(p, row0 + r_tile, n_tile, slot);
+      const int64_t slot = (EPI == kEpiQkv && sg.k0 == 0 && row_lane) ? g_qkv_slot(p, row0 + r_tile) : -1;
+      if (sg.k0 == 0 && half == 0 && row_lane) g_prefetch_epilogue<BN, EPI>(p, row0 + r_tile, n_tile, slot);
       // every epilogue thread reaches the named barriers (all waits are
       // bounded), so the decisions below are uniform over the 4 warps
       if (!mbar_wait(&acc_full[acc], (seg >> 1) & 1, p.status, kGemmKernelId)) *abort_flag = 1;
@@ -612,7 +622,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
         // the tile's XROWS valid rows; after the barrier one thread's release
         // store (cumulative over the CTA's stores ordered by the barrier)
         // raises the flag
-        if (quarter * 32 < XROWS) g_publish<BN, XROWS>(t_row, p, cta, r_tile, half);
+        g_publish<BN, XROWS>(t_row, p, cta, r_tile, half, row_lane);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -640,9 +650,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
         if (ep_tid == 0) g_fetch_partials<BN, XROWS>(p, smem, cta + 1, n_smem, 1, 0, fix_bar);
         if (!mbar_wait(fix_bar, 0, p.status, kGemmKernelId)) n_smem = 0;  // (recorded; sums then incomplete)
       }
-      if (quarter * 32 < XROWS)  // accumulator rows past XROWS hold no data
-        g_tile_epilogue<BN, EPI, XROWS>(p, t_row, stage, quarter, half, lane, row0, n_tile, cta + 1, q_end, 1, 0,
-                                        reinterpret_cast<const float4*>(smem), n_smem, slot);
+      g_tile_epilogue<BN, EPI, XROWS, kRQ>(p, t_row, stage, quarter, half, lane, row0, n_tile, cta + 1, q_end, 1, 0,
+                                           reinterpret_cast<const float4*>(smem), n_smem, slot);
       // every column of this accumulator has been read
       tc_fence_before();
       __syncwarp();
@@ -866,7 +875,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
       if (*abort_flag != 0) break;
       tc_fence_after();
       if (sg.k0 > 0) {
-        g_publish<BN, kGBM>(t_row, p, cta, r_tile, half);
+        g_publish<BN, kGBM>(t_row, p, cta, r_tile, half, true);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(acc_empty_leader[acc]);
@@ -894,7 +903,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
         if (ep_tid == 0) g_fetch_partials<BN, kGBM>(p, smem, pair + 1, n_smem, 2, static_cast<int>(rank), fix_bar);
         if (!mbar_wait(fix_bar, 0, p.status, kGemmKernelId)) n_smem = 0;  // (recorded; sums then incomplete)
       }
-      g_tile_epilogue<BN, EPI, kGBM>(p, t_row, stage, quarter, half, lane, row0, n_tile, pair + 1, q_end, 2,
+      g_tile_epilogue<BN, EPI, kGBM, 32>(p, t_row, stage, quarter, half, lane, row0, n_tile, pair + 1, q_end, 2,
                                static_cast<int>(rank), reinterpret_cast<const float4*>(smem), n_smem, slot);
       tc_fence_before();
       __syncwarp();
