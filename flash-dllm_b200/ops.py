@@ -151,15 +151,17 @@ def _sm_count(index: int) -> int:
 
 def auto_kv_splits(items: int, n_heads: int, max_keys: int, device: torch.device) -> int:
     """Key splits for the attention launch.  The kernel runs one CTA per SM
-    with two work items per CTA; a split count S (1, 2, 4 or 8) runs each
-    pair of items on a cluster of S CTAs, one key slice each, merged in
+    with two work items per CTA; a split count S (1, 2 or 4) runs each pair
+    of items on a cluster of S CTAs, one key slice each, merged in
     distributed shared memory.  Split only while the grid still fits one wave
-    and every slice keeps at least two 64-key tiles."""
+    and every slice keeps at least two 64-key tiles.  Clusters of 8 are left
+    to explicit requests: they measured 2-4 x slower than 4 (one sequence
+    over 640-896 keys: 37.5 vs 14.4-15.7 us)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     sms = _sm_count(idx)
     ctas = max(1, (items + 1) // 2) * n_heads
     s = 1
-    while s < 8 and 2 * s * ctas <= sms and max_keys // (2 * s) >= 128:
+    while s < 4 and 2 * s * ctas <= sms and max_keys // (2 * s) >= 128:
         s *= 2
     return s
 
