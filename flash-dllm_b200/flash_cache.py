@@ -48,12 +48,14 @@ def _own_gemms():
 
 OWN_GEMMS = _own_gemms()
 
-# Rows up to which this package's GEMM measured faster than cuBLAS, per
-# projection (B200, LLaDA-8B shapes, back-to-back launches over weights
-# larger than L2): attn_out 19.0 vs 25.4 us at 64 rows, 25.3 vs 21.0 at 512;
-# the stacked MLP with SwiGLU 47.5 vs 43.1 + 8.2 us (cuBLAS + SwiGLU kernel)
-# at 64 rows, 88.3 vs 77.1 + 10.3 at 512; ff_out 32.1 vs 29.3 at 64.
-_OWN_UP_TO = {"attn_out": 128, "mlp": 1 << 30, "ff_out": 0, "lm_head": 0}
+# Rows up to which this package's GEMM measured at least as fast as cuBLAS,
+# per projection (B200, LLaDA-8B shapes, back-to-back launches over weights
+# larger than L2, one box): attn_out 16.0 vs 25.2 us at 64 rows, 24.1 vs
+# 25.4 at 256, 25.6 vs 25.5 at 512 (cuBLAS down to 21.0 on other boxes);
+# the stacked MLP with SwiGLU 40.7 vs 43.1 + 8.2 us (cuBLAS + SwiGLU kernel)
+# at 64 rows, 88.3 vs 77.1 + 10.3 at 512; ff_out 28.2 vs 28.5 at 64, 31.6 vs
+# 30.2 at 128, 52.2 vs 46.1 at 512.
+_OWN_UP_TO = {"attn_out": 256, "mlp": 1 << 30, "ff_out": 64, "lm_head": 0}
 
 
 def use_own(op: str, rows: int) -> bool:
