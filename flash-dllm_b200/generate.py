@@ -339,6 +339,16 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
             load(j, count)
             count += 1
 
+    def refresh(cont_d, nd_cur_d) -> None:
+        """Reorder each continuing sequence's decoded slots (those decoded
+        before the step's last forward: ``nd_cur_d``) by ascending attention
+        score, then clear the scores -- issued on the device before the
+        step's decisions are read, so the host waits for it in the same read
+        (generate.py:364-381)."""
+        counts = torch.zeros(B, dtype=torch.int64, device=dev).index_copy_(0, act_d, nd_cur_d * cont_d)
+        ops.refresh_sort(full_pos, counts, attn_scores)
+        attn_scores.zero_()
+
     step = 0
     while True:
         act = [j for j in range(B) if st.active[j] != -1]
@@ -399,7 +409,9 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                                                  min_keep, eos_id, full_pos, x, x_draft if verify else None)
         parts = [keep_d.long(), len_d.long(), eos_d]
         if not verify:
-            parts.append(_continues(full_pos, ar_L, act_d, nd_d, keep_d, pred_d, eos_known, eos_d))
+            cont_d = _continues(full_pos, ar_L, act_d, nd_d, keep_d, pred_d, eos_known, eos_d)
+            parts.append(cont_d)
+            refresh(cont_d, nd_d)  # the step's last forward: refresh before the read
         host = d2h(torch.cat(parts))  # one device->host read
         keep1, lnum, eos1 = host[:na], host[na:2 * na], host[2 * na:3 * na]
         cont = host[3 * na:]
@@ -474,6 +486,7 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                 p_tok = torch.zeros(0, dtype=torch.float64, device=dev)
             keep2_d, eos2_d = ops.verify_accept(p_tok, draft_tok, draft_slots, info2_d, eos_known, gamma, eos_id, x)
             cont_d = _continues(full_pos, ar_L, act_d, nd_d, keep2_d, pred_d, eos_known, eos2_d)
+            refresh(cont_d, nd_d)
             host = d2h(torch.cat([keep2_d.long(), eos2_d, cont_d]))
             keep2, eos2, cont = host[:na], host[na:2 * na], host[2 * na:]
             for k, j in enumerate(act):
@@ -481,20 +494,12 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                 if st.eos[j] == -1 and eos2[k] >= 0:
                     st.eos[j] = eos2[k]
                     st.pred[j] = eos2[k] + 1
-            last_keep = keep2
             rec.update(verify_s=dict(zip(act, s_list)), verify_keep=dict(zip(act, keep2)))
-        else:
-            last_keep = keep1
 
         for j in act:
             n_steps[st.active[j]] += 1
 
         # -------------------------------------------- refresh / finish --
-        counts = np.zeros(B, np.int64)
-        for k, j in enumerate(act):
-            if cont[k]:
-                counts[j] = st.nd[j] - last_keep[k]
-        ops.refresh_sort(full_pos, h2d(torch.from_numpy(counts)), attn_scores)
         for k, j in enumerate(act):
             nd = st.nd[j]
             if cont[k]:
@@ -532,7 +537,6 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         if trace is not None:
             rec["nd"] = list(st.nd)
             trace.append(rec)
-        attn_scores.zero_()
         step += 1
         io["steps"] += 1
         if step_hook is not None:
