@@ -34,6 +34,8 @@ def _ab(rows, n, k, seed):
 @pytest.mark.parametrize("rows,n,k,plan", [
     (64, 4096, 4096, {}),               # attn_out, one sequence per GPU
     (64, 4096, 12288, {}),              # ff_out, one sequence per GPU (many pieces per tile)
+    (20, 4096, 12288, {"ksub": 1}),     # M = 64 UMMAs with rows in two of the four TMEM lane quarters
+    (49, 512, 1024, {"bn": 256}),       # ... a row quarter cut inside, 256-column tiles
     (512, 4096, 12288, {}),             # ff_out, eight sequences
     (512, 4096, 4096, {"pair": 0, "bn": 128}),  # single CTAs above 128 rows
     (256, 2048, 2048, {"ksub": 1}),            # CTA pairs, one 64-K box per stage
@@ -86,6 +88,7 @@ def test_gemm_strided_output_and_lm_head_width(gemm_plan):
     (64, 12288, 4096, {}),              # LLaDA-8B MLP, one sequence per GPU
     (512, 12288, 4096, {}),             # eight sequences
     (37, 512, 256, {"bn": 256}),
+    (50, 2048, 1024, {"ksub": 1}),      # M = 64 UMMAs, several pieces per tile
     (200, 1024, 512, {"grid": 5}),
     (200, 1024, 512, {"pair": 0}),
 ])
