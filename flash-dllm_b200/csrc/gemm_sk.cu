@@ -82,7 +82,9 @@ struct GemmParams {
   int32_t m_tiles;
   int32_t n_tiles;
   int32_t kbt;       // k-blocks (KSUB x 64) per tile
-  int32_t iters;     // iterations per group: n_tiles * kbt (x m_tiles with one group)
+  int32_t iters;     // stream-K iterations per group: sk_tiles * kbt
+  int32_t sk_tiles;  // the group's first sk_tiles tiles are split in k-blocks over its CTAs
+  int32_t tiles;     // tiles per group: n_tiles (x m_tiles with one group)
   int32_t epi;
   int32_t d_model;   // QKV: columns per projection
   int32_t hidden;    // swiglu: H (first up row of the stacked weight)
@@ -118,6 +120,36 @@ __device__ __forceinline__ bool g_next(int& i, int hi, int kbt, GSeg& s) {
   s.k1 = s.k0 + (hi - i) < kbt ? s.k0 + (hi - i) : kbt;
   i += s.k1 - s.k0;
   return true;
+}
+
+// The work of CTA (or pair) idx of a group, in order: its even share of the
+// stream-K region (the group's first sk_tiles tiles, k-block range
+// [i, hi) = [g_lo(idx), g_lo(idx + 1)) of sk_tiles * kbt), then the whole tiles
+// sk_tiles + idx, sk_tiles + idx + per_group, ... (data-parallel waves).
+// The stream-K pieces come first so that their fix-up epilogues run while
+// the whole tiles' MMAs stream; only the last whole tile's epilogue is left
+// after the last MMA.
+struct GIter {
+  int i, hi, dp;
+};
+
+// (WAVES false: no whole-tile waves; the plan then puts every tile in the
+// stream-K region, and the kernel carries none of this state)
+template <bool WAVES>
+__device__ __forceinline__ bool g_step(GIter& it, const GemmParams& p, int per_group, GSeg& s) {
+  if (g_next(it.i, it.hi, p.kbt, s)) return true;
+  if (!WAVES || it.dp >= p.tiles) return false;
+  s.tile = it.dp;
+  s.k0 = 0;
+  s.k1 = p.kbt;
+  it.dp += per_group;
+  return true;
+}
+
+// whether segments follow the last one g_step returned
+template <bool WAVES>
+__device__ __forceinline__ bool g_more(const GIter& it, const GemmParams& p) {
+  return it.i < it.hi || (WAVES && it.dp < p.tiles);
 }
 
 // Two 32-column chunks (ca, cb) with their partial sums: both TMEM loads and
@@ -461,7 +493,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
   const int per_group = gridDim.x / p.groups;
   const int group = cta / per_group;  // the m-tile (one group: m-tiles innermost in the tile index)
   const int idx = cta % per_group;    // rank within the group
-  const int lo = g_lo(idx, per_group, p.iters);
+  const int lo = g_lo(idx, per_group, p.iters);  // stream-K range
   const int hi = g_lo(idx + 1, per_group, p.iters);
   const int m_tiles_in = p.groups > 1 ? 1 : p.m_tiles;
 
@@ -509,9 +541,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
   };
   uint32_t n_pre = 0;
   if (warp == 0 && lane == 0) {
-    int i = lo;
+    GIter it{lo, hi, p.sk_tiles + idx};
     GSeg sg;
-    while (n_pre < static_cast<uint32_t>(C::kStages) && g_next(i, hi, p.kbt, sg))
+    while (n_pre < static_cast<uint32_t>(C::kStages) && g_step<false>(it, p, per_group, sg))
       for (int kb = sg.k0; kb < sg.k1 && n_pre < static_cast<uint32_t>(C::kStages); ++kb, ++n_pre) {
         mbar_arrive_expect_tx(&full[n_pre], kTx);
         load_b(sg.tile / m_tiles_in, kb, static_cast<int>(n_pre));
@@ -527,9 +559,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
     if (lane == 0) {
       uint32_t g = 0;
       bool ok = true;
-      int i = lo;
+      GIter it{lo, hi, p.sk_tiles + idx};
       GSeg sg;
-      while (ok && g_next(i, hi, p.kbt, sg)) {
+      while (ok && g_step<false>(it, p, per_group, sg)) {
         const int m_tile = p.groups > 1 ? group : sg.tile % m_tiles_in, n_tile = sg.tile / m_tiles_in;
         for (int kb = sg.k0; kb < sg.k1; ++kb, ++g) {
           const int s = g % C::kStages;
@@ -556,9 +588,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
       uint32_t g = 0;
       int seg = 0;
       bool ok = true;
-      int i = lo;
+      GIter it{lo, hi, p.sk_tiles + idx};
       GSeg sg;
-      while (ok && g_next(i, hi, p.kbt, sg)) {
+      while (ok && g_step<false>(it, p, per_group, sg)) {
         const int acc = seg & 1;
         if (seg >= 2 && !mbar_wait(&acc_empty[acc], ((seg >> 1) & 1) ^ 1, p.status, kGemmKernelId)) break;
         tc_fence_after();
@@ -601,9 +633,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
     const int ep_tid = threadIdx.x - 128;
     float4* stage = stage_all + (warp - 4) * (32 * 16);
     int seg = 0;
-    int i = lo;
+    GIter it{lo, hi, p.sk_tiles + idx};
     GSeg sg;
-    while (g_next(i, hi, p.kbt, sg)) {
+    while (g_step<false>(it, p, per_group, sg)) {
       const int acc = seg & 1;
       const int m_tile = p.groups > 1 ? group : sg.tile % m_tiles_in, n_tile = sg.tile / m_tiles_in;
       const int row0 = m_tile * kGBM;
@@ -644,8 +676,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
         asm volatile("bar.sync 1, 256;" ::: "memory");
         if (*abort_flag != 0) break;
       }
+      // contributors' partials go to the operand ring when it is idle (this
+      // is the CTA's last segment); otherwise they are read from the workspace
       int n_smem = 0;
-      if (q_end > cta + 1) {
+      if (q_end > cta + 1 && !g_more<false>(it, p)) {
         n_smem = min(q_end - cta - 1, C::kBarOffset / (XROWS * BN * 4));
         if (ep_tid == 0) g_fetch_partials<BN, XROWS>(p, smem, cta + 1, n_smem, 1, 0, fix_bar);
         if (!mbar_wait(fix_bar, 0, p.status, kGemmKernelId)) n_smem = 0;  // (recorded; sums then incomplete)
@@ -697,7 +731,7 @@ struct G2Cfg {
   static_assert(kSmem <= 232448, "shared memory");
 };
 
-template <int KSUB, int EPI>
+template <int KSUB, int EPI, bool WAVES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
     gemm_sk2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b0,
                     const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_b2,
@@ -769,9 +803,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
   };
   uint32_t n_pre = 0;
   if (warp == 0 && lane == 0) {
-    int i = lo;
+    GIter it{lo, hi, p.sk_tiles + idx};
     GSeg sg;
-    while (n_pre < static_cast<uint32_t>(C::kStages) && g_next(i, hi, p.kbt, sg))
+    while (n_pre < static_cast<uint32_t>(C::kStages) && g_step<WAVES>(it, p, per_group, sg))
       for (int kb = sg.k0; kb < sg.k1 && n_pre < static_cast<uint32_t>(C::kStages); ++kb, ++n_pre) {
         if (rank == 0) mbar_arrive_expect_tx(&full[n_pre], 2u * C::kStageBytes);
         load_b(sg.tile / m_tiles_in, kb, static_cast<int>(n_pre));
@@ -787,9 +821,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
     if (lane == 0) {
       uint32_t g = 0;
       bool ok = true;
-      int i = lo;
+      GIter it{lo, hi, p.sk_tiles + idx};
       GSeg sg;
-      while (ok && g_next(i, hi, p.kbt, sg)) {
+      while (ok && g_step<WAVES>(it, p, per_group, sg)) {
         const int m_tile = p.groups > 1 ? group : sg.tile % m_tiles_in, n_tile = sg.tile / m_tiles_in;
         const int a_row = m_tile * 2 * kGBM + static_cast<int>(rank) * kGBM;
         for (int kb = sg.k0; kb < sg.k1; ++kb, ++g) {
@@ -817,9 +851,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
       uint32_t g = 0;
       int seg = 0;
       bool ok = true;
-      int i = lo;
+      GIter it{lo, hi, p.sk_tiles + idx};
       GSeg sg;
-      while (ok && g_next(i, hi, p.kbt, sg)) {
+      while (ok && g_step<WAVES>(it, p, per_group, sg)) {
         const int acc = seg & 1;
         if (seg >= 2 && !mbar_wait(&acc_empty[acc], ((seg >> 1) & 1) ^ 1, p.status, kGemmKernelId)) break;
         tc_fence_after();
@@ -861,9 +895,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
     float4* stage = stage_all + (warp - 4) * (32 * 16);
     const uint32_t acc_empty_leader[2] = {mapa_shared(&acc_empty[0], 0), mapa_shared(&acc_empty[1], 0)};
     int seg = 0;
-    int i = lo;
+    GIter it{lo, hi, p.sk_tiles + idx};
     GSeg sg;
-    while (g_next(i, hi, p.kbt, sg)) {
+    while (g_step<WAVES>(it, p, per_group, sg)) {
       const int acc = seg & 1;
       const int m_tile = p.groups > 1 ? group : sg.tile % m_tiles_in, n_tile = sg.tile / m_tiles_in;
       const int row0 = m_tile * 2 * kGBM + static_cast<int>(rank) * kGBM;
@@ -898,7 +932,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
         if (*abort_flag != 0) break;
       }
       int n_smem = 0;
-      if (q_end > pair + 1) {
+      if (q_end > pair + 1 && !g_more<WAVES>(it, p)) {
         n_smem = min(q_end - pair - 1, C::kBarOffset / (kGBM * BN * 4));
         if (ep_tid == 0) g_fetch_partials<BN, kGBM>(p, smem, pair + 1, n_smem, 2, static_cast<int>(rank), fix_bar);
         if (!mbar_wait(fix_bar, 0, p.status, kGemmKernelId)) n_smem = 0;  // (recorded; sums then incomplete)
@@ -930,7 +964,7 @@ namespace {
 struct GemmPlan {
   bool pair;  // CTA-pair kernel (256-row tiles)
   int bn, xrows, ksub, grid, groups;
-  int m_tiles, n_tiles, kbt, iters;
+  int m_tiles, n_tiles, kbt, iters, sk_tiles, tiles;
 };
 
 // Plan overrides for tuning and tests (fdllm_gemm_set_plan): 0 / -1 = automatic.
@@ -952,15 +986,18 @@ int g2_max_pairs() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   if (cache[dev] == 0) {
     using C = G2Cfg<KSUB>;
-    if (cudaFuncSetAttribute(gemm_sk2_kernel<KSUB, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_sk2_kernel<KSUB, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::kSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_sk2_kernel<KSUB, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::kSmem) != cudaSuccess)
       return 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2, 1, 1);
     cfg.blockDim = dim3(kGThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmem;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, gemm_sk2_kernel<KSUB, EPI>, &cfg) != cudaSuccess || n <= 0) return 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_sk2_kernel<KSUB, EPI, false>, &cfg) != cudaSuccess || n <= 0)
+      return 0;
     cache[dev] = n;
   }
   return cache[dev];
@@ -984,7 +1021,7 @@ GemmPlan plan_gemm(int epi, int32_t n_rows, int32_t n_cols, int32_t k_dim, int32
   GemmPlan pl{};
   const GemmOverride& ov = gemm_override();
   const int out_cols = epi == kEpiSwiglu ? n_cols / 2 : n_cols;
-  bool dp = ov.dp > 0;
+  bool dp = ov.dp == 1;
   if (ov.pair < 0 && ov.dp == 0 && n_rows > kGBM && k_dim <= 4096) {
     const long long tiles128 = static_cast<long long>((n_rows + kGBM - 1) / kGBM) *
                                ((out_cols + (epi == kEpiSwiglu ? 63 : 127)) / (epi == kEpiSwiglu ? 64 : 128));
@@ -1019,13 +1056,33 @@ GemmPlan plan_gemm(int epi, int32_t n_rows, int32_t n_cols, int32_t k_dim, int32
   if (units > (pl.pair ? 512 : 1024)) units = pl.pair ? 512 : 1024;
   pl.groups = pl.m_tiles <= units ? pl.m_tiles : 1;
   const long long iters = static_cast<long long>(pl.groups > 1 ? 1 : pl.m_tiles) * pl.n_tiles * pl.kbt;
-  pl.iters = iters > (1ll << 30) ? -1 : static_cast<int>(iters);
+  if (iters > (1ll << 30)) {
+    pl.iters = -1;
+    return pl;
+  }
   int per_group = units / pl.groups;
-  if (pl.iters > 0 && per_group > pl.iters) per_group = pl.iters;
+  if (per_group > iters) per_group = static_cast<int>(iters);
   // data-parallel: at most one whole tile per CTA (no fix-ups) when the
   // tiles fit the grid
   const int tiles_per_group = pl.groups > 1 ? pl.n_tiles : pl.m_tiles * pl.n_tiles;
   if (dp && tiles_per_group <= per_group) per_group = tiles_per_group;
+  // CTA pairs: whole-tile waves plus a stream-K region of the remaining
+  // tiles (split first, so only the last whole tile's epilogue follows the
+  // last MMA; measured 4 and 3 us faster for the QKV and MLP GEMMs at 512
+  // rows; single CTAs, whose tile epilogues are shorter, measured no gain);
+  // a region of fewer than per_group / 8 tiles (pieces under 1/8 of a tile)
+  // takes one wave of whole tiles in with it (so does one with fewer
+  // k-blocks than CTAs: every CTA's range must be non-empty).  dp = 2: all
+  // tiles stream-K.
+  int sk_tiles = tiles_per_group;
+  if (pl.pair && ov.dp != 2 && tiles_per_group >= per_group) {
+    sk_tiles = tiles_per_group % per_group;
+    if (sk_tiles > 0 && (8 * sk_tiles < per_group || static_cast<long long>(sk_tiles) * pl.kbt < per_group))
+      sk_tiles += per_group;
+  }
+  pl.sk_tiles = sk_tiles;
+  pl.tiles = tiles_per_group;
+  pl.iters = sk_tiles * pl.kbt;
   pl.grid = per_group * pl.groups * (pl.pair ? 2 : 1);
   return pl;
 }
@@ -1059,9 +1116,13 @@ int launch_gemm2_cfg(const CUtensorMap& ma, const CUtensorMap& mb0, const CUtens
   using C = G2Cfg<KSUB>;
   if (g2_max_pairs<KSUB, EPI>() <= 0) return FDLLM_ERR_CUDA;  // also sets the shared-memory attribute
   // the kernel's __cluster_dims__ gives the pairs; no cluster attribute here
-  if (launch_ex(gemm_sk2_kernel<KSUB, EPI>, dim3(grid), dim3(kGThreads), C::kSmem, stream, 1, pdl_enabled(), ma, mb0,
-                mb1, mb2, p) != cudaSuccess)
-    return FDLLM_ERR_CUDA;
+  const cudaError_t e =
+      p.sk_tiles < p.tiles
+          ? launch_ex(gemm_sk2_kernel<KSUB, EPI, true>, dim3(grid), dim3(kGThreads), C::kSmem, stream, 1,
+                      pdl_enabled(), ma, mb0, mb1, mb2, p)
+          : launch_ex(gemm_sk2_kernel<KSUB, EPI, false>, dim3(grid), dim3(kGThreads), C::kSmem, stream, 1,
+                      pdl_enabled(), ma, mb0, mb1, mb2, p);
+  if (e != cudaSuccess) return FDLLM_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
 }
 
@@ -1089,7 +1150,7 @@ int run_gemm(int epi, const void* a, int64_t lda, const void* const* w, int n_w,
              int32_t n_cols, int32_t k_dim, GemmParams& p, void* workspace, size_t workspace_bytes,
              cudaStream_t stream) {
   const GemmPlan pl = plan_gemm(epi, n_rows, n_cols, k_dim, p.d_model);
-  if (pl.iters <= 0 || pl.grid <= 0) return FDLLM_ERR_ARG;
+  if (pl.iters < 0 || pl.tiles <= 0 || pl.grid <= 0) return FDLLM_ERR_ARG;
   if (workspace == nullptr || workspace_bytes < gemm_ws_bytes(pl) || !aligned16(workspace))
     return FDLLM_ERR_WORKSPACE;
   p.groups = pl.groups;
@@ -1099,6 +1160,8 @@ int run_gemm(int epi, const void* a, int64_t lda, const void* const* w, int n_w,
   p.n_tiles = pl.n_tiles;
   p.kbt = pl.kbt;
   p.iters = pl.iters;
+  p.sk_tiles = pl.sk_tiles;
+  p.tiles = pl.tiles;
   p.epi = epi;
   p.flags = static_cast<int32_t*>(workspace);
   p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kGFlagBytes);
@@ -1154,7 +1217,7 @@ extern "C" {
 
 int fdllm_gemm_set_plan(int32_t bn, int32_t ksub, int32_t grid, int32_t pair, int32_t dp) {
   if ((bn != 0 && bn != 128 && bn != 256) || (ksub != 0 && ksub != 1 && ksub != 2) || grid < 0 || grid > 1024 ||
-      pair < -1 || pair > 1 || dp < 0 || dp > 1)
+      pair < -1 || pair > 1 || dp < 0 || dp > 2)
     return FDLLM_ERR_ARG;
   fdllm::GemmOverride& o = fdllm::gemm_override();
   o.bn = bn;

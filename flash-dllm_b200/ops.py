@@ -69,8 +69,9 @@ def set_qkv_plan(impl: int = -1, bn: int = 0, splits: int = 0, ksub: int = 0, pa
 
 def set_gemm_plan(bn: int = 0, ksub: int = 0, grid: int = 0, pair: int = -1, dp: int = 0) -> None:
     """Override the stream-K GEMM's tile width, ring stage depth, grid,
-    CTA-pair mode and whole-tile (data-parallel) mode (tuning and tests);
-    no arguments restore the automatic plan."""
+    CTA-pair mode and tile schedule (dp 1: one whole tile per CTA, 2: all
+    tiles split stream-K; tuning and tests); no arguments restore the
+    automatic plan."""
     call("fdllm_gemm_set_plan", bn, ksub, grid, pair, dp)
 
 

@@ -84,10 +84,12 @@ int fdllm_qkv_set_plan(int32_t impl, int32_t bn, int32_t splits, int32_t ksub, i
 
 /* Override the stream-K GEMM's plan (tuning and tests): bn = single-CTA tile width 128 or 256
  * columns, ksub = 64-wide K sub-tiles per ring stage 1 or 2, grid = CTAs or CTA pairs (at most
- * what is resident at once), pair = CTA-pair kernel with 256 x 256 tiles: 1 on, 0 off, dp = 1:
- * one whole tile per CTA (no stream-K pieces) when the tiles fit the grid; 0 / -1 = automatic
- * (pairs above 128 rows, stream-K).  Initial values from FDLLM_GEMM_BN / _KSUB / _GRID / _PAIR /
- * _DP, read once.  No reference counterpart. */
+ * what is resident at once), pair = CTA-pair kernel with 256 x 256 tiles: 1 on, 0 off, -1
+ * automatic (pairs above 128 rows); dp = 1: one whole tile per CTA (no stream-K pieces) when the
+ * tiles fit the grid, 2: every tile split stream-K, 0 = automatic (whole-tile waves after a
+ * stream-K region of the remaining tiles when there are at least as many tiles as CTAs, else
+ * stream-K).  Initial values from FDLLM_GEMM_BN / _KSUB / _GRID / _PAIR / _DP, read once.  No
+ * reference counterpart. */
 int fdllm_gemm_set_plan(int32_t bn, int32_t ksub, int32_t grid, int32_t pair, int32_t dp);
 
 /* Workspace (bytes) of fdllm_gemm_bf16 (swiglu = 0; n_cols = output columns) or

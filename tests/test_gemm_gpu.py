@@ -51,6 +51,13 @@ def _ab(rows, n, k, seed):
     (100, 4096, 1024, {"grid": 30}),    # several contributors per tile, more than fit the ring
     (256, 2048, 2048, {"pair": 0, "bn": 256, "ksub": 1}),
     (64, 2048, 2048, {"bn": 256, "ksub": 2}),
+    # CTA pairs, whole-tile waves after a stream-K region: owners whose
+    # fix-up is not their last segment read the partials from the workspace
+    (512, 12288, 4096, {}),             # QKV width, eight sequences: 22 split tiles + one wave of 74 pairs
+    (512, 12288, 4096, {"dp": 2}),      # ... all tiles stream-K
+    (200, 2048, 1024, {"grid": 3}),     # 2 split tiles over 3 pairs, then 2 waves
+    (100, 2048, 1024, {"grid": 5, "pair": 0}),  # single CTAs (always all stream-K): 16 tiles over 5 CTAs
+    (50, 2048, 1024, {"grid": 6, "ksub": 1}),   # ... M = 64 accumulators
 ])
 @pytest.mark.parametrize("residual", [False, True])
 def test_gemm_matches_torch(rows, n, k, plan, residual, gemm_plan):
@@ -91,6 +98,8 @@ def test_gemm_strided_output_and_lm_head_width(gemm_plan):
     (50, 2048, 1024, {"ksub": 1}),      # M = 64 UMMAs, several pieces per tile
     (200, 1024, 512, {"grid": 5}),
     (200, 1024, 512, {"pair": 0}),
+    (64, 12288, 4096, {"dp": 2}),       # all tiles stream-K (the default has a wave of whole tiles)
+    (300, 2048, 1024, {"grid": 3}),     # pairs, two m-tiles: split tiles then waves
 ])
 def test_gemm_swiglu_matches_torch(rows, h, k, plan, gemm_plan):
     from flash_dllm_b200 import ops
