@@ -21,8 +21,8 @@ residual add, ``ff_proj``/``up_proj`` as one GEMM over the stacked
 activations never reach HBM), and ``ff_out`` with the residual add.
 Each projection runs on the GEMM that measured faster at its row count
 (``use_own``): this package's for the stacked MLP projection at every row
-count and for ``attn_out`` up to 128 rows; cuBLAS (``addmm``, residual in
-its epilogue too) for ``ff_out`` and for ``attn_out`` above 128 rows.  The
+count, for ``attn_out`` up to 256 rows, ``ff_out`` up to 64 and the LM head
+up to 256; cuBLAS (``addmm``, residual in its epilogue too) above.  The
 environment variable ``FDLLM_OWN_GEMMS`` (a comma list of ``attn_out``,
 ``mlp``, ``ff_out``, ``lm_head``, ``all`` or ``none``) forces the choice for
 comparisons (``lm_head``: the model's LM head, in ``model.py``).
@@ -53,9 +53,12 @@ OWN_GEMMS = _own_gemms()
 # larger than L2, one box): attn_out 16.0 vs 25.2 us at 64 rows, 24.1 vs
 # 25.4 at 256, 25.6 vs 25.5 at 512 (cuBLAS down to 21.0 on other boxes);
 # the stacked MLP with SwiGLU 40.7 vs 43.1 + 8.2 us (cuBLAS + SwiGLU kernel)
-# at 64 rows, 88.3 vs 77.1 + 10.3 at 512; ff_out 28.2 vs 28.5 at 64, 31.6 vs
-# 30.2 at 128, 52.2 vs 46.1 at 512.
-_OWN_UP_TO = {"attn_out": 256, "mlp": 1 << 30, "ff_out": 64, "lm_head": 0}
+# at 64 rows, 84.7 vs 77.1 + 10.3 at 512; ff_out 28.2 vs 28.5 at 64, 31.6 vs
+# 30.2 at 128, 50.9 vs 46.1 at 512; the LM head (126464 x 4096) 172.1 vs
+# 179.9 us at 64 rows, 185.6 vs 187.3 at 128, 221.3 vs 198.4 at 192, 231.4
+# vs 241.5 at 256, 383.9 vs 286.0 at 320 (the decode loop's LM-head rows:
+# 32 masked rows per sequence, at most 16 drafts per sequence).
+_OWN_UP_TO = {"attn_out": 256, "mlp": 1 << 30, "ff_out": 64, "lm_head": 256}
 
 
 def use_own(op: str, rows: int) -> bool:
