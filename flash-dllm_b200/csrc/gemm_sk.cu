@@ -1013,9 +1013,9 @@ int g2_max_pairs_for(int epi, int ksub) {
 // streams weights from HBM; narrower tiles give more tiles, so fewer
 // stream-K pieces per tile).  Above: CTA pairs with 256 x 256 tiles, stream-K
 // (bound by operand ingress per SM, which a pair halves for B) -- except
-// short-K problems whose 128 x 128 tiles all fit the grid at once (attn_out:
-// 4096 x 4096 at up to 4 x 128 rows), which run one whole tile per CTA with
-// no fix-ups.  Ring stages: two 64-K boxes (256 B of every operand row per
+// short-K problems whose 128 x 128 tiles fit the grid at once: single CTAs,
+// one whole tile each with no fix-ups when the tiles nearly fill the grid
+// (attn_out: 4096 x 4096 at 4 x 128 rows), stream-K otherwise.  Ring stages: two 64-K boxes (256 B of every operand row per
 // request) for 64-row single CTAs, one 64-K box elsewhere.
 GemmPlan plan_gemm(int epi, int32_t n_rows, int32_t n_cols, int32_t k_dim, int32_t d_model) {
   GemmPlan pl{};
@@ -1023,9 +1023,13 @@ GemmPlan plan_gemm(int epi, int32_t n_rows, int32_t n_cols, int32_t k_dim, int32
   const int out_cols = epi == kEpiSwiglu ? n_cols / 2 : n_cols;
   bool dp = ov.dp == 1;
   if (ov.pair < 0 && ov.dp == 0 && n_rows > kGBM && k_dim <= 4096) {
+    // whole tiles only when they nearly fill one wave: with fewer, stream-K
+    // over all SMs measured faster (attn_out 4096 x 4096: 64 tiles at 256
+    // rows 20.1 vs 23.7 us, 96 at 384 rows 22.7 vs 24.6; 128 at 448-512
+    // rows 24.6 vs 26.2 with whole tiles)
     const long long tiles128 = static_cast<long long>((n_rows + kGBM - 1) / kGBM) *
                                ((out_cols + (epi == kEpiSwiglu ? 63 : 127)) / (epi == kEpiSwiglu ? 64 : 128));
-    if (tiles128 <= sm_count()) dp = true;
+    if (tiles128 <= sm_count() && 5 * tiles128 >= 4ll * sm_count()) dp = true;
   }
   pl.pair = ov.pair < 0 ? (n_rows > kGBM && !dp) : ov.pair != 0;
   if (epi == kEpiQkv && d_model % 256 != 0) pl.pair = false;  // a pair tile holds two heads of one projection

@@ -21,8 +21,8 @@ residual add, ``ff_proj``/``up_proj`` as one GEMM over the stacked
 activations never reach HBM), and ``ff_out`` with the residual add.
 Each projection runs on the GEMM that measured faster at its row count
 (``use_own``): this package's for the stacked MLP projection at every row
-count, for ``attn_out`` up to 256 rows, ``ff_out`` up to 64 and the LM head
-up to 256; cuBLAS (``addmm``, residual in its epilogue too) above.  The
+count, for ``attn_out`` up to 256 rows and ``ff_out`` up to 64; cuBLAS
+(``addmm``, residual in its epilogue too) above and for the LM head.  The
 environment variable ``FDLLM_OWN_GEMMS`` (a comma list of ``attn_out``,
 ``mlp``, ``ff_out``, ``lm_head``, ``all`` or ``none``) forces the choice for
 comparisons (``lm_head``: the model's LM head, in ``model.py``).
@@ -50,15 +50,22 @@ OWN_GEMMS = _own_gemms()
 
 # Rows up to which this package's GEMM measured at least as fast as cuBLAS,
 # per projection (B200, LLaDA-8B shapes, back-to-back launches over weights
-# larger than L2, one box): attn_out 16.0 vs 25.2 us at 64 rows, 24.1 vs
-# 25.4 at 256, 25.6 vs 25.5 at 512 (cuBLAS down to 21.0 on other boxes);
+# larger than L2, one box): attn_out 16.0 vs 25.2 us at 64 rows, 20.1 vs
+# 25.4 at 256, 22.7 vs 25.5 at 384, 24.6 vs 25.5 at 512 (cuBLAS ``addmm``
+# copies the residual into its output first), but inside the power-capped
+# config-4 step (512 rows) this package's attn_out made the step 2.7 %
+# slower (435.4 / 436.2 vs 446.7 / 448.7 tokens/s, alternating runs on one
+# box), so cuBLAS keeps it above 256 rows;
 # the stacked MLP with SwiGLU 40.7 vs 43.1 + 8.2 us (cuBLAS + SwiGLU kernel)
 # at 64 rows, 84.7 vs 77.1 + 10.3 at 512; ff_out 28.2 vs 28.5 at 64, 31.6 vs
 # 30.2 at 128, 50.9 vs 46.1 at 512; the LM head (126464 x 4096) 172.1 vs
 # 179.9 us at 64 rows, 185.6 vs 187.3 at 128, 221.3 vs 198.4 at 192, 231.4
 # vs 241.5 at 256, 383.9 vs 286.0 at 320 (the decode loop's LM-head rows:
-# 32 masked rows per sequence, at most 16 drafts per sequence).
-_OWN_UP_TO = {"attn_out": 256, "mlp": 1 << 30, "ff_out": 64, "lm_head": 256}
+# 32 masked rows per sequence, at most 16 drafts per sequence); in the
+# config-4 step this package's LM head measured 439.8 / 440.2 tokens/s
+# against 441.3 / 446.6 with cuBLAS (alternating runs on one box), so the
+# LM head stays on cuBLAS (``FDLLM_OWN_GEMMS=...,lm_head`` switches it).
+_OWN_UP_TO = {"attn_out": 256, "mlp": 1 << 30, "ff_out": 64, "lm_head": 0}
 
 
 def use_own(op: str, rows: int) -> bool:

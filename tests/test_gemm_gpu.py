@@ -48,6 +48,8 @@ def _ab(rows, n, k, seed):
     (300, 512, 256, {"grid": 2}),       # more m-tiles than CTAs: one group, m-tiles innermost
     (512, 4096, 4096, {"pair": 0, "dp": 1}),  # one whole tile per CTA (128 tiles)
     (512, 4096, 4096, {"dp": 1}),       # CTA pairs, one whole tile each
+    (384, 4096, 4096, {}),              # short K, 96 tiles of 128: single CTAs, stream-K (no whole tiles)
+    (448, 4096, 4096, {}),              # ... 128 tiles: one whole tile per CTA
     (100, 4096, 1024, {"grid": 30}),    # several contributors per tile, more than fit the ring
     (256, 2048, 2048, {"pair": 0, "bn": 256, "ksub": 1}),
     (64, 2048, 2048, {"bn": 256, "ksub": 2}),
@@ -98,7 +100,7 @@ def test_gemm_strided_output_and_lm_head_width(gemm_plan):
     (50, 2048, 1024, {"ksub": 1}),      # M = 64 UMMAs, several pieces per tile
     (200, 1024, 512, {"grid": 5}),
     (200, 1024, 512, {"pair": 0}),
-    (64, 12288, 4096, {"dp": 2}),       # all tiles stream-K (the default has a wave of whole tiles)
+    (64, 12288, 4096, {"dp": 2}),       # the explicit all-stream-K schedule on single CTAs
     (300, 2048, 1024, {"grid": 3}),     # pairs, two m-tiles: split tiles then waves
 ])
 def test_gemm_swiglu_matches_torch(rows, h, k, plan, gemm_plan):
