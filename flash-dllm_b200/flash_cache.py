@@ -14,15 +14,17 @@ The attention half runs on this package's sm_100a kernels: RMSNorm, the
 tcgen05 QKV + RoPE + cache-scatter GEMM (or its verify variant), and one
 fused masked + tracked attention pass (or the verify attention).  The
 reference's ``S`` tensor and ``attn_scores += S.mean((0, 1))`` become an
-in-kernel accumulation.  After attention the projections run on the
+in-kernel accumulation.  After attention the projections can run on the
 package's stream-K tcgen05 GEMM with fused epilogues: ``attn_out`` with the
 residual add, ``ff_proj``/``up_proj`` as one GEMM over the stacked
 ``ffup_weight`` whose epilogue forms bf16(silu(gate)) * up (the gate and up
 activations never reach HBM), and ``ff_out`` with the residual add.
 Each projection runs on the GEMM that measured faster at its row count
-(``use_own``): this package's for the stacked MLP projection at every row
-count, for ``attn_out`` up to 256 rows and ``ff_out`` up to 64; cuBLAS
-(``addmm``, residual in its epilogue too) above and for the LM head.  The
+(``use_own``): this package's for the stacked MLP projection up to 256
+rows; cuBLAS (``addmm``, residual in its epilogue too) for
+``attn_out``, ``ff_out``, the LM head and the MLP above 256 rows: in the
+full decode step those measured faster (this package's kernels are faster
+alone at several of those shapes).  The
 environment variable ``FDLLM_OWN_GEMMS`` (a comma list of ``attn_out``,
 ``mlp``, ``ff_out``, ``lm_head``, ``all`` or ``none``) forces the choice for
 comparisons (``lm_head``: the model's LM head, in ``model.py``).
@@ -48,24 +50,38 @@ def _own_gemms():
 
 OWN_GEMMS = _own_gemms()
 
-# Rows up to which this package's GEMM measured at least as fast as cuBLAS,
-# per projection (B200, LLaDA-8B shapes, back-to-back launches over weights
-# larger than L2, one box): attn_out 16.0 vs 25.2 us at 64 rows, 20.1 vs
-# 25.4 at 256, 22.7 vs 25.5 at 384, 24.6 vs 25.5 at 512 (cuBLAS ``addmm``
-# copies the residual into its output first), but inside the power-capped
-# config-4 step (512 rows) this package's attn_out made the step 2.7 %
-# slower (435.4 / 436.2 vs 446.7 / 448.7 tokens/s, alternating runs on one
-# box), so cuBLAS keeps it above 256 rows;
-# the stacked MLP with SwiGLU 40.7 vs 43.1 + 8.2 us (cuBLAS + SwiGLU kernel)
-# at 64 rows, 84.7 vs 77.1 + 10.3 at 512; ff_out 28.2 vs 28.5 at 64, 31.6 vs
-# 30.2 at 128, 50.9 vs 46.1 at 512; the LM head (126464 x 4096) 172.1 vs
-# 179.9 us at 64 rows, 185.6 vs 187.3 at 128, 221.3 vs 198.4 at 192, 231.4
-# vs 241.5 at 256, 383.9 vs 286.0 at 320 (the decode loop's LM-head rows:
-# 32 masked rows per sequence, at most 16 drafts per sequence); in the
-# config-4 step this package's LM head measured 439.8 / 440.2 tokens/s
-# against 441.3 / 446.6 with cuBLAS (alternating runs on one box), so the
-# LM head stays on cuBLAS (``FDLLM_OWN_GEMMS=...,lm_head`` switches it).
-_OWN_UP_TO = {"attn_out": 256, "mlp": 1 << 30, "ff_out": 64, "lm_head": 0}
+# Rows up to which this package's GEMM is used, per projection, chosen by
+# alternating full-step runs on one B200 (generated tokens/s; kernel timings
+# taken alone ranked several of these the other way: back-to-back launches
+# of one of this package's kernels overlap each launch's prologue and first
+# weight loads with the tail of the one before, which the step's neighbours
+# do not allow, and the config-4 step runs at the power cap).  Config 4
+# (512-row forwards): cuBLAS for attn_out, the MLP projection and the LM head
+# 449.4 / 448.7 vs 439.1 / 439.0 with this package's attn_out (kernel alone
+# 24.6 vs 25.5 us) and MLP + SwiGLU (84.7 vs 77.1 + 10.3 us); config 3
+# (64-row forwards): cuBLAS attn_out and ff_out with this package's MLP
+# 227.2 / 227.3 vs 217.1 / 221.3 with this package's ff_out and 208.3 / 211.6
+# with its attn_out too (alone 16.0 vs 25.2 us), while the MLP on cuBLAS
+# lost 4.5 % (205.3 vs 214.8); config 5 (384 / 256 rows): cuBLAS attn_out
+# 246.7 / 246.2 vs 240.0 / 241.5, the MLP even.  The QKV projection has no
+# cuBLAS counterpart (RoPE and the cache scatter are in its epilogue).
+_OWN_UP_TO = {"attn_out": 0, "mlp": 256, "ff_out": 0, "lm_head": 0}
+
+
+def _own_up_to_env() -> None:
+    """``FDLLM_OWN_UP_TO`` (e.g. ``mlp:128,attn_out:0``) overrides row
+    thresholds of the table above (tuning runs)."""
+    v = os.environ.get("FDLLM_OWN_UP_TO")
+    if not v:
+        return
+    for item in v.split(","):
+        name, _, rows = item.partition(":")
+        if name.strip() not in _OWN_UP_TO:
+            raise ValueError(f"FDLLM_OWN_UP_TO: unknown projection {name!r}")
+        _OWN_UP_TO[name.strip()] = int(rows)
+
+
+_own_up_to_env()
 
 
 def use_own(op: str, rows: int) -> bool:
