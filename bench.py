@@ -181,15 +181,44 @@ class _Clocks:
 def _rot_time(fns, reps=3):
     """Mean per-launch time (s) of back-to-back launches cycling through
     `fns` (each over its own inputs, together larger than L2), CUDA events
-    on the current stream."""
+    on the launching stream.  The cycle is captured once as a CUDA graph and
+    replayed, so the host's per-call launch cost (Python, ctypes, torch
+    dispatch: 10-25 us) does not pace kernels shorter than that; without a
+    graph (a call that cannot be captured) the launches are issued eagerly."""
     for f in fns:
         f()
+    torch.cuda.synchronize()
+    graph = None
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            g.capture_begin()
+            try:
+                for f in fns:
+                    f()
+            finally:
+                g.capture_end()
+        graph = g
+    except RuntimeError:
+        graph = None
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+
+    def cycle():
+        if graph is not None:
+            graph.replay()
+        else:
+            for f in fns:
+                f()
+
+    cycle()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(reps):
-        for f in fns:
-            f()
+        cycle()
     b.record()
     b.synchronize()
     return a.elapsed_time(b) * 1e-3 / (reps * len(fns))
