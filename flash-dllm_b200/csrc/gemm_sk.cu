@@ -270,56 +270,70 @@ __device__ __forceinline__ void g_stage_get8(const float4* stage, int r, int u, 
 template <int BN, int EPI, int PR, int RQ>
 __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_row, float4* stage, int quarter,
                                                 int half, int lane, int row0, int n_tile, int q0, int q1, int qmul,
-                                                int qadd, const float4* spart, int n_smem, int64_t slot) {
+                                                int qadd, const float4* spart, int n_smem, int64_t slot,
+                                                float4* stage2) {
   const int r_tile = quarter * RQ + (lane < RQ ? lane : 0);
   const int wrow0 = row0 + quarter * RQ;  // global row of the warp's staged row 0
   if (EPI == kEpiQkv) {
+    // 4 lanes per staged row: lane takes head columns c .. c + 7 (c = 32 half
+    // + 8 sub) and their RoPE partners c + 64 ..; two rows per batch, their
+    // table loads in flight together.  Both heads of a 256-column tile share
+    // the rows' tables: with a second staging area free (`stage2`: the
+    // operand ring after the CTA's last MMA) the two heads are staged
+    // together and each row batch's tables are loaded once for both.
+    const int sub = lane & 3;
+    const int c = half * 32 + 8 * sub;
+    constexpr int kHeads = BN / 128;
+    const int group = (kHeads == 2 && stage2 != nullptr) ? 2 : 1;
 #pragma unroll 1
-    for (int hh = 0; hh < BN / 128; ++hh) {
-      const int n0 = n_tile * BN + hh * 128;
-      const int proj = n0 / p.d_model;
-      const int hcol = n0 - proj * p.d_model;  // first column of the head in its projection
-      __nv_bfloat16* out = proj == 0 ? p.out0 : (proj == 1 ? p.out1 : p.out2);
-      const bool by_slot = proj > 0 && p.kv_by_slot;
-      {
-        const int ch = half;
+    for (int h0 = 0; h0 < kHeads; h0 += group) {
+#pragma unroll 1
+      for (int g = 0; g < group; ++g) {
+        const int hh = h0 + g;
         float va[32], vb[32];
-        g_chunk2<BN, PR>(t_row, hh * 128 + ch * 32, hh * 128 + 64 + ch * 32, p, q0, q1, qmul, qadd, spart, n_smem, r_tile,
-                     va, vb);
-        g_stage_put(stage, lane, va, vb);
-        __syncwarp();
-        // 4 lanes per row: lane takes head columns c .. c + 7 (c = ch * 32 +
-        // 8 sub) and their RoPE partners c + 64 ..; two rows per batch, their
-        // table loads in flight together
-        const int sub = lane & 3;
-        const int c = ch * 32 + 8 * sub;
+        g_chunk2<BN, PR>(t_row, hh * 128 + half * 32, hh * 128 + 64 + half * 32, p, q0, q1, qmul, qadd, spart,
+                         n_smem, r_tile, va, vb);
+        g_stage_put(g == 0 ? stage : stage2, lane, va, vb);
+      }
+      __syncwarp();
+      // the group's first head has the lowest projection: tables are needed
+      // unless it is a V head
+      const bool rope = (n_tile * BN + h0 * 128) / p.d_model < 2;
 #pragma unroll 1
-        for (int it = 0; it < RQ / 8; it += 2) {
-          int64_t sl[2];
-          float4 tb[2][8];
+      for (int it = 0; it < RQ / 8; it += 2) {
+        int64_t sl[2];
+        float4 tb[2][8];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            sl[u] = __shfl_sync(0xffffffffu, slot, (it + u) * 8 + (lane >> 2));
-            const int64_t sr = sl[u] < 0 ? 0 : sl[u];
-            const float4* sp = reinterpret_cast<const float4*>(p.sin + sr * 128 + c);
-            const float4* cp = reinterpret_cast<const float4*>(p.cos + sr * 128 + c);
-            if (proj < 2) {
-              tb[u][0] = __ldg(sp);
-              tb[u][1] = __ldg(sp + 1);
-              tb[u][2] = __ldg(sp + 16);
-              tb[u][3] = __ldg(sp + 17);
-              tb[u][4] = __ldg(cp);
-              tb[u][5] = __ldg(cp + 1);
-              tb[u][6] = __ldg(cp + 16);
-              tb[u][7] = __ldg(cp + 17);
-            }
+        for (int u = 0; u < 2; ++u) {
+          sl[u] = __shfl_sync(0xffffffffu, slot, (it + u) * 8 + (lane >> 2));
+          const int64_t sr = sl[u] < 0 ? 0 : sl[u];
+          const float4* sp = reinterpret_cast<const float4*>(p.sin + sr * 128 + c);
+          const float4* cp = reinterpret_cast<const float4*>(p.cos + sr * 128 + c);
+          if (rope) {
+            tb[u][0] = __ldg(sp);
+            tb[u][1] = __ldg(sp + 1);
+            tb[u][2] = __ldg(sp + 16);
+            tb[u][3] = __ldg(sp + 17);
+            tb[u][4] = __ldg(cp);
+            tb[u][5] = __ldg(cp + 1);
+            tb[u][6] = __ldg(cp + 16);
+            tb[u][7] = __ldg(cp + 17);
           }
+        }
+#pragma unroll 1
+        for (int g = 0; g < group; ++g) {
+          const int n0 = n_tile * BN + (h0 + g) * 128;
+          const int proj = n0 / p.d_model;
+          const int hcol = n0 - proj * p.d_model;  // first column of the head in its projection
+          __nv_bfloat16* out = proj == 0 ? p.out0 : (proj == 1 ? p.out1 : p.out2);
+          const bool by_slot = proj > 0 && p.kv_by_slot;
+          const float4* st = g == 0 ? stage : stage2;
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int rr = (it + u) * 8 + (lane >> 2);
             float x1[8], x2[8];
-            g_stage_get8(stage, rr, 2 * sub, x1);
-            g_stage_get8(stage, rr, 8 + 2 * sub, x2);
+            g_stage_get8(st, rr, 2 * sub, x1);
+            g_stage_get8(st, rr, 8 + 2 * sub, x2);
             if (sl[u] < 0) continue;
             if (proj < 2) {
               const float s1[8] = {tb[u][0].x, tb[u][0].y, tb[u][0].z, tb[u][0].w,
@@ -343,8 +357,8 @@ __device__ __forceinline__ void g_tile_epilogue(const GemmParams& p, uint32_t t_
             *reinterpret_cast<uint4*>(dst + 64) = g_pack8(x2);
           }
         }
-        __syncwarp();
       }
+      __syncwarp();
     }
   } else if (EPI == kEpiStore) {
 #pragma unroll 1
@@ -684,8 +698,12 @@ __global__ void __launch_bounds__(kGThreads, 1)
         if (ep_tid == 0) g_fetch_partials<BN, XROWS>(p, smem, cta + 1, n_smem, 1, 0, fix_bar);
         if (!mbar_wait(fix_bar, 0, p.status, kGemmKernelId)) n_smem = 0;  // (recorded; sums then incomplete)
       }
+      // after the CTA's last MMA the operand ring is free unless it holds
+      // contributors' partials: a second staging area for the QKV epilogue
+      float4* stage2 = (!g_more<false>(it, p) && q_end == cta + 1)
+                           ? reinterpret_cast<float4*>(smem) + (warp - 4) * (32 * 16) : nullptr;
       g_tile_epilogue<BN, EPI, XROWS, kRQ>(p, t_row, stage, quarter, half, lane, row0, n_tile, cta + 1, q_end, 1, 0,
-                                           reinterpret_cast<const float4*>(smem), n_smem, slot);
+                                           reinterpret_cast<const float4*>(smem), n_smem, slot, stage2);
       // every column of this accumulator has been read
       tc_fence_before();
       __syncwarp();
@@ -937,8 +955,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
         if (ep_tid == 0) g_fetch_partials<BN, kGBM>(p, smem, pair + 1, n_smem, 2, static_cast<int>(rank), fix_bar);
         if (!mbar_wait(fix_bar, 0, p.status, kGemmKernelId)) n_smem = 0;  // (recorded; sums then incomplete)
       }
+      // after the pair's last MMA (its completion reached both CTAs) the
+      // operand ring is free unless it holds contributors' partials
+      float4* stage2 = (!g_more<WAVES>(it, p) && q_end == pair + 1)
+                           ? reinterpret_cast<float4*>(smem) + (warp - 4) * (32 * 16) : nullptr;
       g_tile_epilogue<BN, EPI, kGBM, 32>(p, t_row, stage, quarter, half, lane, row0, n_tile, pair + 1, q_end, 2,
-                               static_cast<int>(rank), reinterpret_cast<const float4*>(smem), n_smem, slot);
+                               static_cast<int>(rank), reinterpret_cast<const float4*>(smem), n_smem, slot, stage2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty_leader[acc]);
