@@ -1125,10 +1125,11 @@ int fdllm_verify_qkv(const void* xn, const void* wq, const void* wk, const void*
 //
 //  * The array is kQkvNoAllocScratchBytes (24 MiB) of global memory on every
 //    GPU that loads the library, held until the process exits.
-//  * Requests whose split-K scratch would exceed it are refused with
-//    FDLLM_ERR_SCRATCH_LIMIT before anything is launched (for LLaDA-8B,
-//    d_model 4096, that is any call of more than 128 query rows; calls that
-//    need no split, such as 512 rows, use no scratch and are accepted).
+//  * Requests whose scratch would exceed it are refused with
+//    FDLLM_ERR_SCRATCH_LIMIT before anything is launched.  For LLaDA-8B
+//    (d_model 4096) the stream-K GEMM, the default at every row count,
+//    needs at most its flags plus one 128 KB partial per CTA (about 19 MB)
+//    and fits; the earlier kernels' requested K splits above 128 rows do not.
 //  * The first call on a device resolves the array's device address
 //    (cudaGetSymbolAddress, with that device current); make that first call
 //    before any stream capture.
