@@ -70,7 +70,7 @@ WORKLOADS = {
 # DRAM bytes (read + write) of one launch, from an ncu capture of that kernel
 # at that row count (the per-kernel summaries give the commands); emitted
 # only for the captured shape.
-NCU_TRAFFIC = {("mlp", 512): 214299904 + 30049024, ("qkv", 512): 110198272 + 17776896}
+NCU_TRAFFIC = {("mlp", 512): 214299904 + 30049024, ("qkv", 512): 110186496 + 17552896}
 
 
 def _workload(name: str) -> dict:
