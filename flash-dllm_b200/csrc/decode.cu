@@ -313,6 +313,97 @@ __global__ void verify_accept_kernel(const VerifyArgs a) {
   a.eos_out[j] = eos;
 }
 
+// ---------------------------------------------------------- verify build ----
+// The Flash-Verify forward's inputs of one step, built on the device from a
+// few scalars per sequence (the reference builds them per sequence on the
+// host, llada/generate.py:254-292).  seq int64 [n_seq, 8] = (slot row j,
+// drafts s, num decoded nd, seqlen_k, predicted length, key offset, draft
+// offset, unused).  Per sequence, 2 bm verify rows p: the t = 2 bm - 2 s
+// decoded slots before nd (p < t), the s draft slots (t <= p < t + s, tokens
+// from x_draft) and the same s slots again as the mask view (tokens from x);
+// keys: its cache slots [0, nd - t) and [nd + s, seqlen_k); the (2 bm)^2 verify
+// mask; the drafts' slots and logit rows; the attention's block row and the
+// acceptance scan's (offset, s, 0, predicted length) row.
+struct VBuildArgs {
+  const int64_t* seq;
+  const int64_t* full_pos;
+  const int64_t* x;
+  const int64_t* x_draft;
+  int64_t* qpos;
+  int64_t* xv;
+  uint8_t* mask;
+  int64_t* kpos;
+  int64_t* dslot;
+  int64_t* lidx;
+  int32_t* vblocks;
+  int64_t* info2;
+  int32_t* status;
+  int64_t n_slots;
+  int64_t lmax;
+  int32_t bm;
+};
+
+// (the reference's mask, generate.py:262-269: rows of the decoded slots do not
+// see the drafts; drafts and their mask view see each other causally)
+__device__ __forceinline__ uint8_t verify_mask_bit(int r, int c, int t, int s) {
+  if (r < t) return (c >= t && c < t + s) ? 0 : 1;
+  if (c < t || c >= t + 2 * s) return 1;
+  const int rr = r - t, cc = c - t;
+  if (rr < s) return cc < s ? (rr >= cc) : (rr < cc - s);
+  return cc < s ? (rr - s > cc) : (rr - s <= cc - s);
+}
+
+__global__ void __launch_bounds__(256) verify_build_kernel(const VBuildArgs a) {
+  const int k = blockIdx.x;
+  const int64_t* q = a.seq + 8 * static_cast<int64_t>(k);
+  const int64_t j = q[0], s = q[1], nd = q[2], sk = q[3], pred = q[4], koff = q[5], soff = q[6];
+  const int R = 2 * a.bm;
+  const int64_t t = R - 2 * s;
+  const int64_t row0 = j * a.lmax;
+  const int64_t base = row0 + nd;
+  const int64_t len1 = nd - t > 0 ? nd - t : 0;
+  const int64_t len2 = sk - nd - s > 0 ? sk - nd - s : 0;
+  bool bad = s < 0 || t < 0;
+  auto slot_at = [&](int64_t idx) -> int64_t {
+    if (idx < row0 || idx >= row0 + a.lmax || idx >= a.n_slots) {
+      bad = true;
+      return 0;
+    }
+    return a.full_pos[idx];
+  };
+  for (int p = threadIdx.x; p < R && !(s < 0 || t < 0); p += blockDim.x) {
+    const bool draft = p >= t && p < t + s;
+    const int64_t off = p < t + s ? p - t : p - t - s;
+    int64_t slot = slot_at(base + off);
+    if (slot < 0 || slot >= a.n_slots) {
+      bad = true;
+      slot = 0;
+    }
+    a.qpos[static_cast<int64_t>(k) * R + p] = slot;
+    a.xv[static_cast<int64_t>(k) * R + p] = draft ? a.x_draft[slot] : a.x[slot];
+  }
+  for (int e = threadIdx.x; e < R * R; e += blockDim.x)
+    a.mask[(static_cast<int64_t>(k) * R + e / R) * R + e % R] =
+        (s < 0 || t < 0) ? 1 : verify_mask_bit(e / R, e % R, static_cast<int>(t), static_cast<int>(s));
+  for (int64_t i = threadIdx.x; i < s; i += blockDim.x) {
+    a.dslot[soff + i] = slot_at(base + i);
+    a.lidx[soff + i] = static_cast<int64_t>(k) * R + t + s + i;
+  }
+  for (int64_t n = threadIdx.x; n < len1 + len2; n += blockDim.x)
+    a.kpos[koff + n] = slot_at(n < len1 ? row0 + n : base + s + (n - len1));
+  if (threadIdx.x == 0) {
+    a.vblocks[4 * k + 0] = static_cast<int32_t>(koff);
+    a.vblocks[4 * k + 1] = static_cast<int32_t>(koff + len1 + len2);
+    a.vblocks[4 * k + 2] = k * R;
+    a.vblocks[4 * k + 3] = k * R + R;
+    a.info2[4 * k + 0] = soff;
+    a.info2[4 * k + 1] = s;
+    a.info2[4 * k + 2] = 0;
+    a.info2[4 * k + 3] = pred;
+  }
+  if (bad) report(a.status, FDLLM_ERR_INDEX, k, kDecodeKernelId);
+}
+
 // --------------------------------------------------------- refresh sort ----
 // Orderable 32-bit image of a float for ascending order; -0 sorts as +0 and
 // NaN after +inf (torch.sort's placement).
@@ -429,6 +520,21 @@ int fdllm_verify_accept(const double* p, const int64_t* draft_tok, const int64_t
   fdllm::VerifyArgs a{p, draft_tok, draft_slot, seq_info, eos_known, x, keep_out, eos_out, fdllm::status_ptr(),
                       n_slots, eos_id, gamma, batch};
   fdllm::verify_accept_kernel<<<(batch + 127) / 128, 128, 0, stream>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
+}
+
+int fdllm_verify_build(const int64_t* seq, int32_t n_seq, int32_t bm, int64_t lmax, int64_t n_slots,
+                       const int64_t* full_pos, const int64_t* x, const int64_t* x_draft, int64_t* qpos, int64_t* xv,
+                       uint8_t* mask, int64_t* kpos, int64_t* dslot, int64_t* lidx, int32_t* vblocks, int64_t* info2,
+                       cudaStream_t stream) {
+  if (n_seq < 0 || bm <= 0 || bm > 512 || lmax <= 0 || n_slots <= 0) return FDLLM_ERR_ARG;
+  if (n_seq == 0) return FDLLM_OK;
+  const void* ptrs[] = {seq, full_pos, x, x_draft, qpos, xv, mask, vblocks, info2};
+  for (const void* q : ptrs)
+    if (q == nullptr) return FDLLM_ERR_ARG;
+  fdllm::VBuildArgs a{seq,  full_pos, x,     x_draft, qpos, xv, mask, kpos, dslot, lidx, vblocks, info2,
+                      fdllm::status_ptr(), n_slots, lmax, bm};
+  fdllm::verify_build_kernel<<<n_seq, 256, 0, stream>>>(a);
   return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
 }
 

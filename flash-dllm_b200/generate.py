@@ -309,7 +309,6 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
     attn_scores = sess.attn_scores
     rotary_emb_pos = sess.rotary
     empty_i32, empty_i64 = sess.empty_i32, sess.empty_i64
-    masks = [torch.from_numpy(_verify_mask(bm, s)).to(dev) for s in range(bm // 2 + 1)]
     ar_L = torch.arange(L, device=dev)
     st = _Slots(B)
     forward = sess.forward
@@ -428,40 +427,26 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
             # every sequence has 2*bm verify rows: t trailing decoded slots, its
             # s drafts, the same s slots again (mask view); keys are the rest
             # of its cache range
+            # per sequence: its slot row, s drafts, decoded count, key range end,
+            # predicted length and running key / draft offsets; the verify rows,
+            # keys, mask and the acceptance rows are built from these on the
+            # device (fdllm_verify_build)
             s_a = np.array(s_list, np.int64)
             t_a = 2 * bm - 2 * s_a
             nd_a = np.array([st.nd[j] for j in act], np.int64)
             sk_a = np.array([st.seqlen_k[j] for j in act], np.int64)
-            base = np.array(act, np.int64) * L + nd_a
-            P = np.arange(2 * bm, dtype=np.int64)[None, :]
-            T, S = t_a[:, None], s_a[:, None]
-            qi = (base[:, None] + np.where(P < T + S, P - T, P - T - S)).reshape(-1)
-            flags = ((P >= T) & (P < T + S)).reshape(-1)
-            di = qi[flags]
-            logit_idx = np.flatnonzero((P >= T + S).reshape(-1))
-            lens = np.stack([nd_a - t_a, sk_a - nd_a - s_a], 1)
-            ki = _multi_arange(np.stack([base - nd_a, base + s_a], 1).reshape(-1), lens.reshape(-1))
-            nk = np.maximum(lens, 0).sum(1)
-            k_end = np.cumsum(nk)
-            q0 = np.arange(len(act), dtype=np.int64) * 2 * bm
-            vrows = np.stack([k_end - nk, k_end, q0, q0 + 2 * bm], 1)
-            info2 = np.stack([np.cumsum(s_a) - s_a, s_a, np.zeros_like(s_a),
-                              np.array([st.pred[j] for j in act], np.int64)], 1)
+            nk = np.maximum(nd_a - t_a, 0) + np.maximum(sk_a - nd_a - s_a, 0)
+            pred_a = np.array([st.pred[j] for j in act], np.int64)
+            seqtab = np.stack([np.array(act, np.int64), s_a, nd_a, sk_a, pred_a, np.cumsum(nk) - nk,
+                               np.cumsum(s_a) - s_a, np.zeros_like(s_a)], 1)
             pk = _Pack()
-            for part in (qi, ki, di, flags, logit_idx, vrows, info2):
-                pk.add(part)
+            pk.add(seqtab)
             pk.add([1 if st.eos[j] != -1 else 0 for j in act])
-            pk.add([st.nd[j] for j in act])
-            pk.add([st.pred[j] for j in act])
-            qi_d, ki_d, di_d, flag, lidx, vblocks, info2_d, eos_known, nd_d, pred_d = pk.send(h2d)
-            flat_pos = full_pos.view(-1)
-            qpos = flat_pos[qi_d]
-            key_pos_flat = flat_pos[ki_d]
-            draft_slots = flat_pos[di_d]
-            x_verify = torch.where(flag.bool(), x_draft[qpos], x[qpos])
-            attn_mask = torch.cat([masks[s] for s in s_list])
-            vblocks = vblocks.view(-1, 4).to(torch.int32)
-            info2_d = info2_d.view(-1, 4)
+            pk.add(nd_a)
+            pk.add(pred_a)
+            seq_d, eos_known, nd_d, pred_d = pk.send(h2d)
+            qpos, x_verify, attn_mask, key_pos_flat, draft_slots, lidx, vblocks, info2_d = ops.verify_build(
+                seq_d.view(-1, 8), int(nk.sum()), int(s_a.sum()), bm, full_pos, x, x_draft)
             eos_known = eos_known.to(torch.int32)
 
             def verify_forward(t, hook, n_m=n_m):
@@ -470,7 +455,7 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                 return _call_model(model, t["x"].unsqueeze(0), lengths, positions, t["lidx"], hook)
 
             if sum(s_list) > 0:
-                logits_v = forward(("verify", x_verify.numel(), key_pos_flat.numel(), len(vrows), lidx.numel()),
+                logits_v = forward(("verify", x_verify.numel(), key_pos_flat.numel(), len(act), lidx.numel()),
                                    {"x": x_verify, "qpos": qpos, "kpos": key_pos_flat, "mask": attn_mask,
                                     "vblocks": vblocks, "lidx": lidx}, verify_forward)
                 if record is not None:

@@ -360,6 +360,26 @@ def verify_accept(p, draft_tok, draft_slot, seq_info, eos_known, gamma: float, e
     return keep, eos
 
 
+def verify_build(seq: torch.Tensor, n_keys: int, n_drafts: int, bm: int, full_pos: torch.Tensor, x: torch.Tensor,
+                 x_draft: torch.Tensor):
+    """Flash-Verify forward inputs from per-sequence scalars (``seq`` int64
+    [n, 8], see fdllm_verify_build) -> device (qpos, x_verify, mask bool
+    [n * 2bm, 2bm], key slots, draft slots, logit rows, verify blocks int32
+    [n, 4], acceptance rows int64 [n, 4])."""
+    _check(seq, "seq", torch.int64, 2)
+    _check(full_pos, "full_pos", torch.int64, 2)
+    n, dev, r = seq.shape[0], seq.device, 2 * bm
+    i64 = dict(dtype=torch.int64, device=dev)
+    qpos, xv = torch.empty(n * r, **i64), torch.empty(n * r, **i64)
+    mask = torch.empty(n * r, r, dtype=torch.bool, device=dev)
+    kpos, dslot, lidx = torch.empty(n_keys, **i64), torch.empty(n_drafts, **i64), torch.empty(n_drafts, **i64)
+    vblocks = torch.empty(n, 4, dtype=torch.int32, device=dev)
+    info2 = torch.empty(n, 4, **i64)
+    call("fdllm_verify_build", ptr(seq), n, bm, full_pos.shape[1], x.numel(), ptr(full_pos), ptr(x), ptr(x_draft),
+         ptr(qpos), ptr(xv), ptr(mask), ptr(kpos), ptr(dslot), ptr(lidx), ptr(vblocks), ptr(info2), _stream())
+    return qpos, xv, mask, kpos, dslot, lidx, vblocks, info2
+
+
 def refresh_sort(full_pos: torch.Tensor, counts: torch.Tensor, scores: torch.Tensor) -> None:
     """In place: full_pos[j, :counts[j]] ordered by ascending score (stable)."""
     _check(full_pos, "full_pos", torch.int64, 2)

@@ -258,6 +258,22 @@ int fdllm_verify_accept(const double* p, const int64_t* draft_tok, const int64_t
                         double gamma, int64_t eos_id, int64_t* x, int32_t* keep_out, int64_t* eos_out,
                         cudaStream_t stream);
 
+/* Flash-Verify forward inputs of one step, built on the device from per-sequence scalars.
+ * seq int64 [n_seq, 8] = (slot row j, drafts s <= bm, num decoded nd, seqlen_k, predicted length,
+ * key offset, draft offset, unused); the offsets are the running sums of the key counts
+ * max(nd - t, 0) + max(seqlen_k - nd - s, 0) (t = 2 bm - 2 s) and of s.  full_pos int64 [n_seq rows of
+ * lmax] (the slot order), x / x_draft int64 [n_slots].  Writes per sequence k: qpos / xv int64
+ * [k * 2bm .. + 2bm) (verify rows' slots and tokens: t decoded slots before nd, the s drafts from
+ * x_draft, the same s slots from x), mask uint8 [2bm rows x 2bm] (the verify mask), kpos int64 (its
+ * keys: slots full_pos[j, 0:nd - t] and full_pos[j, nd + s:seqlen_k]), dslot / lidx int64 [s] (the
+ * drafts' slots and logit rows), vblocks int32 [4] (key begin, key end, row begin, row end) and
+ * info2 int64 [4] (draft offset, s, 0, predicted length).  Indices outside the sequence's row are
+ * reported as FDLLM_ERR_INDEX.  ref llada/generate.py:254-292 (verify inputs), :262-269 (mask). */
+int fdllm_verify_build(const int64_t* seq, int32_t n_seq, int32_t bm, int64_t lmax, int64_t n_slots,
+                       const int64_t* full_pos, const int64_t* x, const int64_t* x_draft, int64_t* qpos, int64_t* xv,
+                       uint8_t* mask, int64_t* kpos, int64_t* dslot, int64_t* lidx, int32_t* vblocks, int64_t* info2,
+                       cudaStream_t stream);
+
 /* Top-k selective refresh order: for each sequence j, stably sort full_pos[j, 0:counts[j]]
  * (int64 [batch, lmax]) ascending by scores[full_pos[j, i]] in place (counts[j] <= 8192).
  * ref llada/generate.py:364-366. */

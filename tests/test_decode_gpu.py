@@ -174,3 +174,64 @@ def test_refresh_sort_matches_stable_oracle(n_max):
         head = ref[j, :n]
         ref[j, :n] = head[do.refresh_order(sc[head])]
     assert torch.equal(fp.cpu(), ref)
+
+
+def _host_verify_build(act, s_a, nd_a, sk_a, pred_a, bm, L, full_pos, x, x_draft):
+    """The Flash-Verify inputs built on the host with numpy, the way the
+    decode loop built them before (a batched restatement of
+    llada/generate.py:254-292): the reference for fdllm_verify_build."""
+    from oracle.decode_oracle import verify_mask
+    act, s_a, nd_a, sk_a, pred_a = (np.asarray(v, np.int64) for v in (act, s_a, nd_a, sk_a, pred_a))
+    t_a = 2 * bm - 2 * s_a
+    base = act * L + nd_a
+    P = np.arange(2 * bm, dtype=np.int64)[None, :]
+    T, S = t_a[:, None], s_a[:, None]
+    qi = (base[:, None] + np.where(P < T + S, P - T, P - T - S)).reshape(-1)
+    flags = ((P >= T) & (P < T + S)).reshape(-1)
+    lidx = np.flatnonzero((P >= T + S).reshape(-1))
+    lens = np.maximum(np.stack([nd_a - t_a, sk_a - nd_a - s_a], 1), 0)
+    starts = np.stack([base - nd_a, base + s_a], 1)
+    ki = np.concatenate([np.arange(a, a + n) for a, n in zip(starts.reshape(-1), lens.reshape(-1))]
+                        + [np.zeros(0, np.int64)])
+    nk = lens.sum(1)
+    k_end = np.cumsum(nk)
+    q0 = np.arange(len(act), dtype=np.int64) * 2 * bm
+    vrows = np.stack([k_end - nk, k_end, q0, q0 + 2 * bm], 1).astype(np.int32)
+    info2 = np.stack([np.cumsum(s_a) - s_a, s_a, np.zeros_like(s_a), pred_a], 1)
+    flat = full_pos.reshape(-1)
+    qpos = flat[qi]
+    xv = np.where(flags, x_draft[qpos], x[qpos])
+    mask = np.concatenate([np.asarray(verify_mask(bm, int(s)).numpy(), bool) for s in s_a])
+    return qpos, xv, mask, flat[ki], flat[qi[flags]], lidx, vrows, info2
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_verify_build_matches_host_build(seed):
+    """fdllm_verify_build against the host build on random decode states
+    (active slot subsets, 0 .. bm/2 drafts, decoded counts near and far from
+    the key range end, permuted slot orders): every output bit-exact."""
+    import flash_dllm_b200.ops as ops
+    from flash_dllm_b200._lib import check_device_status
+    rng = np.random.default_rng(seed)
+    B, L, bm = 8, 512, 32
+    full_pos = np.stack([rng.permutation(L) + j * L for j in range(B)]).astype(np.int64)
+    x = rng.integers(0, 126464, B * L).astype(np.int64)
+    x_draft = rng.integers(0, 126464, B * L).astype(np.int64)
+    act = sorted(rng.choice(B, size=int(rng.integers(1, B + 1)), replace=False).tolist())
+    s_a = rng.integers(0, bm // 2 + 1, len(act))
+    s_a[0] = 0
+    sk_a = rng.choice([384, 448, 512], len(act))
+    nd_a = np.array([int(rng.integers(2 * bm, sk - s)) for sk, s in zip(sk_a, s_a)])
+    pred_a = rng.integers(256, L, len(act))
+    ref = _host_verify_build(act, s_a, nd_a, sk_a, pred_a, bm, L, full_pos, x, x_draft)
+    t_a = 2 * bm - 2 * s_a
+    nk = np.maximum(nd_a - t_a, 0) + np.maximum(sk_a - nd_a - s_a, 0)
+    seq = np.stack([np.asarray(act), s_a, nd_a, sk_a, pred_a, np.cumsum(nk) - nk, np.cumsum(s_a) - s_a,
+                    np.zeros_like(s_a)], 1).astype(np.int64)
+    dev = torch.device("cuda")
+    got = ops.verify_build(torch.from_numpy(seq).to(dev), int(nk.sum()), int(s_a.sum()), bm,
+                           torch.from_numpy(full_pos).to(dev), torch.from_numpy(x).to(dev),
+                           torch.from_numpy(x_draft).to(dev))
+    check_device_status()
+    for name, r, g in zip(("qpos", "x_verify", "mask", "kpos", "draft_slots", "lidx", "vblocks", "info2"), ref, got):
+        assert np.array_equal(g.cpu().numpy(), np.asarray(r)), name
