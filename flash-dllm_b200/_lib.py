@@ -51,6 +51,7 @@ SIGNATURES = {
     "fdllm_window_accept": (_int, [_p, _p, _p, _p, _p, _i32, _i64, _i64, _f64, _i32, _i64, _p, _p, _p, _p, _p, _p,
                                    _p]),
     "fdllm_verify_accept": (_int, [_p, _p, _p, _p, _p, _i32, _i64, _f64, _i64, _p, _p, _p, _p]),
+    "fdllm_cache_build": (_int, [_p, _i32, _i32, _i64, _i64, _p, _p, _p, _p, _p, _p, _p]),
     "fdllm_verify_build": (_int, [_p, _i32, _i32, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "fdllm_refresh_sort": (_int, [_p, _i32, _i64, _p, _p, _i64, _p]),
 }

@@ -404,6 +404,79 @@ __global__ void __launch_bounds__(256) verify_build_kernel(const VBuildArgs a) {
   if (bad) report(a.status, FDLLM_ERR_INDEX, k, kDecodeKernelId);
 }
 
+// ----------------------------------------------------------- cache build ----
+// The Flash-Cache forward's inputs of one step on the device (the reference's
+// block tables and query lists, llada/generate.py:146-163, 439-465).  seq int64
+// [n_seq, 16] = (slot row j, k_end, num decoded nd, predicted length, masked
+// range start, masked count, tracked range 1 start, count, tracked range 2
+// start, count, masked row offset, tracked row offset, masked tile offset,
+// tracked tile offset, unused, unused); positions are indices into row j of
+// full_pos.  Writes the sequence's query rows (slots and tokens: its masked
+// rows among the first rows of the row space, its tracked rows after all
+// masked ones), its block-table rows (seq, k_end, row begin, row end) in
+// tiles of bm rows, and its window-acceptance row (masked row offset,
+// masked count, flat index of nd, predicted length).
+struct CBuildArgs {
+  const int64_t* seq;
+  const int64_t* full_pos;
+  const int64_t* x;
+  int64_t* tables;
+  int64_t* qpos;
+  int64_t* xq;
+  int64_t* seq_info;
+  int32_t* status;
+  int64_t n_slots;
+  int64_t lmax;
+  int32_t bm;
+};
+
+__global__ void __launch_bounds__(256) cache_build_kernel(const CBuildArgs a) {
+  const int k = blockIdx.x;
+  const int64_t* q = a.seq + 16 * static_cast<int64_t>(k);
+  const int64_t j = q[0], k_end = q[1], nd = q[2], pred = q[3];
+  const int64_t ma = q[4], mn = q[5], t1a = q[6], t1n = q[7], t2a = q[8], t2n = q[9];
+  const int64_t mo = q[10], to = q[11], mt = q[12], tt = q[13];
+  const int64_t row0 = j * a.lmax, tn = t1n + t2n;
+  bool bad = false;
+  auto put = [&](int64_t row, int64_t pos) {
+    int64_t slot = 0;
+    if (pos < 0 || pos >= a.lmax || row0 + pos >= a.n_slots) {
+      bad = true;
+    } else {
+      slot = a.full_pos[row0 + pos];
+      if (slot < 0 || slot >= a.n_slots) {
+        bad = true;
+        slot = 0;
+      }
+    }
+    a.qpos[row] = slot;
+    a.xq[row] = a.x[slot];
+  };
+  for (int64_t i = threadIdx.x; i < mn; i += blockDim.x) put(mo + i, ma + i);
+  for (int64_t i = threadIdx.x; i < tn; i += blockDim.x) put(to + i, i < t1n ? t1a + i : t2a + (i - t1n));
+  for (int64_t u = threadIdx.x; u * a.bm < mn; u += blockDim.x) {
+    int64_t* r = a.tables + 4 * (mt + u);
+    r[0] = j;
+    r[1] = k_end;
+    r[2] = mo + u * a.bm;
+    r[3] = mo + ((u + 1) * a.bm < mn ? (u + 1) * a.bm : mn);
+  }
+  for (int64_t u = threadIdx.x; u * a.bm < tn; u += blockDim.x) {
+    int64_t* r = a.tables + 4 * (tt + u);
+    r[0] = j;
+    r[1] = k_end;
+    r[2] = to + u * a.bm;
+    r[3] = to + ((u + 1) * a.bm < tn ? (u + 1) * a.bm : tn);
+  }
+  if (threadIdx.x == 0) {
+    a.seq_info[4 * k + 0] = mo;
+    a.seq_info[4 * k + 1] = mn;
+    a.seq_info[4 * k + 2] = row0 + nd;
+    a.seq_info[4 * k + 3] = pred;
+  }
+  if (bad) report(a.status, FDLLM_ERR_INDEX, k, kDecodeKernelId);
+}
+
 // --------------------------------------------------------- refresh sort ----
 // Orderable 32-bit image of a float for ascending order; -0 sorts as +0 and
 // NaN after +inf (torch.sort's placement).
@@ -535,6 +608,19 @@ int fdllm_verify_build(const int64_t* seq, int32_t n_seq, int32_t bm, int64_t lm
   fdllm::VBuildArgs a{seq,  full_pos, x,     x_draft, qpos, xv, mask, kpos, dslot, lidx, vblocks, info2,
                       fdllm::status_ptr(), n_slots, lmax, bm};
   fdllm::verify_build_kernel<<<n_seq, 256, 0, stream>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
+}
+
+int fdllm_cache_build(const int64_t* seq, int32_t n_seq, int32_t bm, int64_t lmax, int64_t n_slots,
+                      const int64_t* full_pos, const int64_t* x, int64_t* tables, int64_t* qpos, int64_t* xq,
+                      int64_t* seq_info, cudaStream_t stream) {
+  if (n_seq < 0 || bm <= 0 || lmax <= 0 || n_slots <= 0) return FDLLM_ERR_ARG;
+  if (n_seq == 0) return FDLLM_OK;
+  const void* ptrs[] = {seq, full_pos, x, seq_info};
+  for (const void* q : ptrs)
+    if (q == nullptr) return FDLLM_ERR_ARG;
+  fdllm::CBuildArgs a{seq, full_pos, x, tables, qpos, xq, seq_info, fdllm::status_ptr(), n_slots, lmax, bm};
+  fdllm::cache_build_kernel<<<n_seq, 256, 0, stream>>>(a);
   return cudaPeekAtLastError() == cudaSuccess ? FDLLM_OK : FDLLM_ERR_CUDA;
 }
 

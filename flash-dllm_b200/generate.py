@@ -31,7 +31,7 @@ tokens per step; ``trace`` (a list) receives the per-step decisions.
 """
 from __future__ import annotations
 
-from typing import List, Optional
+from typing import Optional
 
 import weakref
 
@@ -56,11 +56,6 @@ def make_blocks(j: int, seqlen_k, max_length, start_m: int, end_m: int, block_m:
     q_ends = q_starts + block_m
     q_ends[-1] = end_m
     return torch.stack((torch.full_like(q_starts, j), torch.full_like(q_starts, seqlen_k[j]), q_starts, q_ends), 1)
-
-
-def _tiles(rows: List, j: int, k_end: int, start: int, n: int, bm: int) -> None:
-    for s in range(start, start + n, bm):
-        rows.append((j, k_end, s, min(s + bm, start + n)))
 
 
 class _Forwarder:
@@ -218,30 +213,6 @@ class _Slots:
         self.tracked = [()] * b  # ((start, end), ...)
 
 
-def _multi_arange(starts, lens) -> np.ndarray:
-    """Concatenation of ``arange(starts[i], starts[i] + lens[i])`` (negative
-    lengths count as 0)."""
-    starts = np.asarray(starts, np.int64)
-    lens = np.maximum(np.asarray(lens, np.int64), 0)
-    total = int(lens.sum())
-    if total == 0:
-        return np.zeros(0, np.int64)
-    ends = np.cumsum(lens)
-    return np.arange(total, dtype=np.int64) + np.repeat(starts - (ends - lens), lens)
-
-
-def _ranges_idx(rows, L: int, ranges) -> np.ndarray:
-    """Flat ``full_pos`` indices of the position ranges of slot rows ``rows``
-    (``ranges[k]`` belongs to row ``rows[k]``), in order."""
-    st = [j * L + a for j, rs in zip(rows, ranges) for a, _ in rs]
-    ln = [b - a for rs in ranges for a, b in rs]
-    return _multi_arange(st, ln)
-
-
-def _count(ranges) -> int:
-    return sum(max(0, b - a) for a, b in ranges)
-
-
 class _Pack:
     """Host arrays sent to the device in one pinned copy; ``views`` returns
     the device tensors in the order they were added."""
@@ -354,44 +325,40 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         if not act:
             break
         # ---------------------------------------------------- Flash-Cache --
-        m_rows, t_rows, acc = [], [], 0
-        m_lens = []
-        for j in act:
-            n = _count(st.masked[j])
-            m_lens.append(n)
-            if n:
-                _tiles(m_rows, j, st.seqlen_k[j], acc, n, bm)
-                acc += n
-        r_m = acc
-        for j in act:
-            n = _count(st.tracked[j])
-            if n:
-                _tiles(t_rows, j, st.seqlen_k[j], acc, n, bm)
-                acc += n
+        # per sequence: its slot row, k_end, nd, predicted length, the masked
+        # range and the (up to two) tracked ranges as positions of its row of
+        # full_pos, and its row / block-table tile offsets (masked rows of all
+        # sequences first, then the tracked rows); the block tables, query
+        # slots and tokens are built from these on the device
+        # (fdllm_cache_build)
         na = len(act)
-        info = np.zeros((na, 4), np.int64)
-        off = 0
+        seqtab = np.zeros((na, 16), np.int64)
         for k, j in enumerate(act):
-            info[k] = (off, m_lens[k], j * L + st.nd[j], st.pred[j])
-            off += m_lens[k]
+            mr, tr = st.masked[j], st.tracked[j]
+            seqtab[k, 0:4] = (j, st.seqlen_k[j], st.nd[j], st.pred[j])
+            for c, (a, b) in zip((4, 6, 8), list(mr[:1]) + [(0, 0)] * (1 - len(mr[:1])) + list(tr[:2])
+                                 + [(0, 0)] * (2 - len(tr[:2]))):
+                seqtab[k, c:c + 2] = (a, max(0, b - a))
+        m_n, t_n = seqtab[:, 5], seqtab[:, 7] + seqtab[:, 9]
+        m_tl, t_tl = -(-m_n // bm), -(-t_n // bm)
+        r_m, n_m = int(m_n.sum()), int(m_tl.sum())
+        seqtab[:, 10] = np.cumsum(m_n) - m_n
+        seqtab[:, 11] = r_m + np.cumsum(t_n) - t_n
+        seqtab[:, 12] = np.cumsum(m_tl) - m_tl
+        seqtab[:, 13] = n_m + np.cumsum(t_tl) - t_tl
+        n_t = int(t_tl.sum())
         pk = _Pack()
-        pk.add(np.array(m_rows + t_rows, np.int64))
-        pk.add(np.concatenate([_ranges_idx(act, L, [st.masked[j] for j in act]),
-                               _ranges_idx(act, L, [st.tracked[j] for j in act])]))
-        pk.add(info)
+        pk.add(seqtab)
         pk.add([1 if st.eos[j] != -1 else 0 for j in act])
         pk.add(act)
-        pk.add([st.nd[j] for j in act])
-        pk.add([st.pred[j] for j in act])
-        tables, qidx, seq_info, eos_known, act_d, nd_d, pred_d = pk.send(h2d)
-        tables = tables.view(-1, 4)
-        seq_info = seq_info.view(-1, 4)
+        pk.add(seqtab[:, 2])
+        pk.add(seqtab[:, 3])
+        seq_d, eos_known, act_d, nd_d, pred_d = pk.send(h2d)
+        tables, query_pos_flat, x_query, seq_info = ops.cache_build(seq_d.view(-1, 16), r_m + int(t_n.sum()),
+                                                                    n_m + n_t, bm, full_pos, x)
         eos_known = eos_known.to(torch.int32)
-        query_pos_flat = full_pos.view(-1)[qidx]
-        x_query = x[query_pos_flat]
-        n_m = len(m_rows)
 
-        def cache_forward(t, hook, n_m=n_m, r_m=r_m, has_t=bool(t_rows)):
+        def cache_forward(t, hook, n_m=n_m, r_m=r_m, has_t=n_t > 0):
             masked_blocks = t["tables"][:n_m] if n_m else empty_i32
             tracked_blocks = t["tables"][n_m:] if has_t else empty_i32
             positions = [t["qpos"], empty_i64, rotary_emb_pos, [], attn_scores, []]
@@ -399,7 +366,7 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                        None, False]
             return _call_model(model, t["x"].unsqueeze(0), lengths, positions, r_m, hook)
 
-        logits = forward(("cache", x_query.numel(), n_m, len(t_rows), r_m),
+        logits = forward(("cache", x_query.numel(), n_m, n_t, r_m),
                          {"x": x_query, "qpos": query_pos_flat, "tables": tables}, cache_forward)
         if record is not None:
             record(False, x_query, query_pos_flat, None, logits, torch.arange(r_m, device=dev), attn_scores)

@@ -360,6 +360,22 @@ def verify_accept(p, draft_tok, draft_slot, seq_info, eos_known, gamma: float, e
     return keep, eos
 
 
+def cache_build(seq: torch.Tensor, n_rows: int, n_tiles: int, bm: int, full_pos: torch.Tensor, x: torch.Tensor):
+    """Flash-Cache forward inputs from per-sequence scalars (``seq`` int64
+    [n, 16], see fdllm_cache_build) -> device (block tables int64
+    [n_tiles, 4], query slots, query tokens, window-acceptance rows [n, 4])."""
+    _check(seq, "seq", torch.int64, 2)
+    _check(full_pos, "full_pos", torch.int64, 2)
+    n, dev = seq.shape[0], seq.device
+    i64 = dict(dtype=torch.int64, device=dev)
+    tables = torch.empty(n_tiles, 4, **i64)
+    qpos, xq = torch.empty(n_rows, **i64), torch.empty(n_rows, **i64)
+    seq_info = torch.empty(n, 4, **i64)
+    call("fdllm_cache_build", ptr(seq), n, bm, full_pos.shape[1], x.numel(), ptr(full_pos), ptr(x), ptr(tables),
+         ptr(qpos), ptr(xq), ptr(seq_info), _stream())
+    return tables, qpos, xq, seq_info
+
+
 def verify_build(seq: torch.Tensor, n_keys: int, n_drafts: int, bm: int, full_pos: torch.Tensor, x: torch.Tensor,
                  x_draft: torch.Tensor):
     """Flash-Verify forward inputs from per-sequence scalars (``seq`` int64

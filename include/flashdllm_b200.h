@@ -258,6 +258,21 @@ int fdllm_verify_accept(const double* p, const int64_t* draft_tok, const int64_t
                         double gamma, int64_t eos_id, int64_t* x, int32_t* keep_out, int64_t* eos_out,
                         cudaStream_t stream);
 
+/* Flash-Cache forward inputs of one step, built on the device from per-sequence scalars.
+ * seq int64 [n_seq, 16] = (slot row j, k_end, num decoded nd, predicted length, masked range start,
+ * masked count, tracked range 1 start, count, tracked range 2 start, count, masked row offset,
+ * tracked row offset, masked tile offset, tracked tile offset, 0, 0); range starts index row j of
+ * full_pos (int64 [n_seq rows of lmax], the slot order); x int64 [n_slots].  Writes the sequence's
+ * query rows to qpos / xq (slots and tokens; masked rows at the masked row offset, tracked rows,
+ * range 1 then 2, at the tracked row offset), its block-table rows (seq, k_end, row begin, row end)
+ * as tiles of bm rows at the tile offsets of tables int64 [tiles, 4], and seq_info int64 [n_seq, 4] =
+ * (masked row offset, masked count, j * lmax + nd, predicted length) for fdllm_window_accept.
+ * Positions outside row j are reported as FDLLM_ERR_INDEX.
+ * ref llada/generate.py:52-58 (make_blocks), :146-163 and :439-465 (masked / tracked block tables). */
+int fdllm_cache_build(const int64_t* seq, int32_t n_seq, int32_t bm, int64_t lmax, int64_t n_slots,
+                      const int64_t* full_pos, const int64_t* x, int64_t* tables, int64_t* qpos, int64_t* xq,
+                      int64_t* seq_info, cudaStream_t stream);
+
 /* Flash-Verify forward inputs of one step, built on the device from per-sequence scalars.
  * seq int64 [n_seq, 8] = (slot row j, drafts s <= bm, num decoded nd, seqlen_k, predicted length,
  * key offset, draft offset, unused); the offsets are the running sums of the key counts

@@ -235,3 +235,90 @@ def test_verify_build_matches_host_build(seed):
     check_device_status()
     for name, r, g in zip(("qpos", "x_verify", "mask", "kpos", "draft_slots", "lidx", "vblocks", "info2"), ref, got):
         assert np.array_equal(g.cpu().numpy(), np.asarray(r)), name
+
+
+def _host_cache_build(act, masked, tracked, seqlen_k, nd, pred, bm, L, full_pos, x):
+    """The Flash-Cache inputs built on the host, the way the decode loop built
+    them before (restating llada/generate.py:52-58, 146-163, 439-465): masked
+    rows of all sequences first, then the tracked rows, in tiles of bm rows;
+    the reference for fdllm_cache_build."""
+    m_rows, t_rows, acc, m_lens = [], [], 0, []
+
+    def tiles(rows, j, start, n):
+        for s0 in range(start, start + n, bm):
+            rows.append((j, seqlen_k[j], s0, min(s0 + bm, start + n)))
+
+    for j in act:
+        n = sum(max(0, b - a) for a, b in masked[j])
+        m_lens.append(n)
+        if n:
+            tiles(m_rows, j, acc, n)
+            acc += n
+    r_m = acc
+    for j in act:
+        n = sum(max(0, b - a) for a, b in tracked[j])
+        if n:
+            tiles(t_rows, j, acc, n)
+            acc += n
+    idx = [j * L + p for rs in (masked, tracked) for j in act for a, b in rs[j] for p in range(a, b)]
+    flat = full_pos.reshape(-1)
+    qpos = flat[np.asarray(idx, np.int64)]
+    info, off = [], 0
+    for k, j in enumerate(act):
+        info.append((off, m_lens[k], j * L + nd[j], pred[j]))
+        off += m_lens[k]
+    return (np.asarray(m_rows + t_rows, np.int64).reshape(-1, 4), qpos, x[qpos], np.asarray(info, np.int64), r_m,
+            len(m_rows), len(t_rows))
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_cache_build_matches_host_build(seed):
+    """fdllm_cache_build against the host build on random decode states: a
+    freshly loaded slot (tracked = the prompt and the tail, a prefill-sized
+    row set), continuing slots (masked window, a tracked window on either
+    side), empty ranges and finished slots; every output bit-exact."""
+    import flash_dllm_b200.ops as ops
+    from flash_dllm_b200._lib import check_device_status
+    rng = np.random.default_rng(seed)
+    B, L, bm = 8, 512, 32
+    full_pos = np.stack([rng.permutation(L) + j * L for j in range(B)]).astype(np.int64)
+    x = rng.integers(0, 126464, B * L).astype(np.int64)
+    act = sorted(rng.choice(B, size=int(rng.integers(1, B + 1)), replace=False).tolist())
+    masked, tracked, seqlen_k, nd, pred = {}, {}, {}, {}, {}
+    for i, j in enumerate(act):
+        sk = int(rng.choice([384, 448, 512]))
+        seqlen_k[j], pred[j] = sk, int(rng.integers(256, L))
+        if i == 0:  # just loaded: prompt p, masked window after it, tracked = the rest
+            p = int(rng.integers(40, 200))
+            nd[j], masked[j], tracked[j] = p, ((p, p + bm),), ((0, p), (p + bm, max(sk, p + bm)))
+        else:
+            d = int(rng.integers(bm, sk - bm))
+            t0 = max(0, d - int(rng.integers(0, 3)) * bm)
+            t1 = min(sk, d + bm * int(rng.integers(1, 3)))
+            nd[j], masked[j] = d, ((d, min(d + bm, L)),)
+            tracked[j] = ((t0, d), (min(d + bm, L), max(t1, min(d + bm, L))))
+    ref_tab, ref_q, ref_x, ref_info, r_m, n_m, n_t = _host_cache_build(act, masked, tracked, seqlen_k, nd, pred, bm, L,
+                                                                      full_pos, x)
+    # the decode loop's per-sequence scalars (flash-dllm_b200/generate.py)
+    seq = np.zeros((len(act), 16), np.int64)
+    for k, j in enumerate(act):
+        seq[k, 0:4] = (j, seqlen_k[j], nd[j], pred[j])
+        rs = list(masked[j][:1]) + [(0, 0)] * (1 - len(masked[j][:1])) + list(tracked[j][:2]) \
+            + [(0, 0)] * (2 - len(tracked[j][:2]))
+        for c, (a, b) in zip((4, 6, 8), rs):
+            seq[k, c:c + 2] = (a, max(0, b - a))
+    m_n, t_n = seq[:, 5], seq[:, 7] + seq[:, 9]
+    m_tl, t_tl = -(-m_n // bm), -(-t_n // bm)
+    seq[:, 10] = np.cumsum(m_n) - m_n
+    seq[:, 11] = m_n.sum() + np.cumsum(t_n) - t_n
+    seq[:, 12] = np.cumsum(m_tl) - m_tl
+    seq[:, 13] = m_tl.sum() + np.cumsum(t_tl) - t_tl
+    assert (int(m_tl.sum()), int(t_tl.sum()), int(m_n.sum())) == (n_m, n_t, r_m)
+    dev = torch.device("cuda")
+    tab, qpos, xq, info = ops.cache_build(torch.from_numpy(seq).to(dev), int(m_n.sum() + t_n.sum()), n_m + n_t, bm,
+                                          torch.from_numpy(full_pos).to(dev), torch.from_numpy(x).to(dev))
+    check_device_status()
+    assert np.array_equal(tab.cpu().numpy(), ref_tab)
+    assert np.array_equal(qpos.cpu().numpy(), ref_q)
+    assert np.array_equal(xq.cpu().numpy(), ref_x)
+    assert np.array_equal(info.cpu().numpy(), ref_info)
