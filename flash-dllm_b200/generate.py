@@ -86,7 +86,8 @@ class _Forwarder:
         if hit is not None:
             static, graphs, out = hit
             for name, t in inputs.items():
-                static[name].copy_(t)
+                if t is not static[name]:  # (built in place by the caller: see static_inputs)
+                    static[name].copy_(t)
             for graph in graphs:
                 graph.replay()
             return out
@@ -120,6 +121,13 @@ class _Forwarder:
         cur.wait_stream(self.stream)
         self.graphs[key] = (static, graphs, out)
         return result
+
+
+    def static_inputs(self, key):
+        """The captured graph's input tensors for ``key`` (None before its
+        capture): a caller may build a step's inputs straight into them."""
+        hit = self.graphs.get(key) if self.enabled else None
+        return None if hit is None else hit[0]
 
 
 class _Staging:
@@ -354,8 +362,11 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
         pk.add(seqtab[:, 2])
         pk.add(seqtab[:, 3])
         seq_d, eos_known, act_d, nd_d, pred_d = pk.send(h2d)
-        tables, query_pos_flat, x_query, seq_info = ops.cache_build(seq_d.view(-1, 16), r_m + int(t_n.sum()),
-                                                                    n_m + n_t, bm, full_pos, x)
+        ckey = ("cache", r_m + int(t_n.sum()), n_m, n_t, r_m)
+        st_in = forward.static_inputs(ckey)
+        tables, query_pos_flat, x_query, seq_info = ops.cache_build(
+            seq_d.view(-1, 16), r_m + int(t_n.sum()), n_m + n_t, bm, full_pos, x,
+            out=None if st_in is None else (st_in["tables"], st_in["qpos"], st_in["x"]))
         eos_known = eos_known.to(torch.int32)
 
         def cache_forward(t, hook, n_m=n_m, r_m=r_m, has_t=n_t > 0):
@@ -366,7 +377,7 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                        None, False]
             return _call_model(model, t["x"].unsqueeze(0), lengths, positions, r_m, hook)
 
-        logits = forward(("cache", x_query.numel(), n_m, n_t, r_m),
+        logits = forward(ckey,
                          {"x": x_query, "qpos": query_pos_flat, "tables": tables}, cache_forward)
         if record is not None:
             record(False, x_query, query_pos_flat, None, logits, torch.arange(r_m, device=dev), attn_scores)
@@ -412,8 +423,12 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
             pk.add(nd_a)
             pk.add(pred_a)
             seq_d, eos_known, nd_d, pred_d = pk.send(h2d)
+            vkey = ("verify", na * 2 * bm, int(nk.sum()), na, int(s_a.sum()))
+            st_in = forward.static_inputs(vkey) if sum(s_list) > 0 else None
             qpos, x_verify, attn_mask, key_pos_flat, draft_slots, lidx, vblocks, info2_d = ops.verify_build(
-                seq_d.view(-1, 8), int(nk.sum()), int(s_a.sum()), bm, full_pos, x, x_draft)
+                seq_d.view(-1, 8), int(nk.sum()), int(s_a.sum()), bm, full_pos, x, x_draft,
+                out=None if st_in is None else (st_in["qpos"], st_in["x"], st_in["mask"], st_in["kpos"],
+                                                st_in["lidx"], st_in["vblocks"]))
             eos_known = eos_known.to(torch.int32)
 
             def verify_forward(t, hook, n_m=n_m):
@@ -422,7 +437,7 @@ def generate_with_Flash_dLLM(model, prompts, prompt_lengths, batch_size, respons
                 return _call_model(model, t["x"].unsqueeze(0), lengths, positions, t["lidx"], hook)
 
             if sum(s_list) > 0:
-                logits_v = forward(("verify", x_verify.numel(), key_pos_flat.numel(), len(act), lidx.numel()),
+                logits_v = forward(vkey,
                                    {"x": x_verify, "qpos": qpos, "kpos": key_pos_flat, "mask": attn_mask,
                                     "vblocks": vblocks, "lidx": lidx}, verify_forward)
                 if record is not None:

@@ -360,16 +360,23 @@ def verify_accept(p, draft_tok, draft_slot, seq_info, eos_known, gamma: float, e
     return keep, eos
 
 
-def cache_build(seq: torch.Tensor, n_rows: int, n_tiles: int, bm: int, full_pos: torch.Tensor, x: torch.Tensor):
+def cache_build(seq: torch.Tensor, n_rows: int, n_tiles: int, bm: int, full_pos: torch.Tensor, x: torch.Tensor,
+                out=None):
     """Flash-Cache forward inputs from per-sequence scalars (``seq`` int64
     [n, 16], see fdllm_cache_build) -> device (block tables int64
-    [n_tiles, 4], query slots, query tokens, window-acceptance rows [n, 4])."""
+    [n_tiles, 4], query slots, query tokens, window-acceptance rows [n, 4]);
+    ``out`` = (tables, query slots, query tokens) to write into."""
     _check(seq, "seq", torch.int64, 2)
     _check(full_pos, "full_pos", torch.int64, 2)
     n, dev = seq.shape[0], seq.device
     i64 = dict(dtype=torch.int64, device=dev)
-    tables = torch.empty(n_tiles, 4, **i64)
-    qpos, xq = torch.empty(n_rows, **i64), torch.empty(n_rows, **i64)
+    if out is None:
+        tables = torch.empty(n_tiles, 4, **i64)
+        qpos, xq = torch.empty(n_rows, **i64), torch.empty(n_rows, **i64)
+    else:
+        tables, qpos, xq = out
+        if tables.shape != (n_tiles, 4) or qpos.numel() != n_rows or xq.numel() != n_rows:
+            raise ValueError("cache_build: output buffers of the wrong size")
     seq_info = torch.empty(n, 4, **i64)
     call("fdllm_cache_build", ptr(seq), n, bm, full_pos.shape[1], x.numel(), ptr(full_pos), ptr(x), ptr(tables),
          ptr(qpos), ptr(xq), ptr(seq_info), _stream())
@@ -377,19 +384,27 @@ def cache_build(seq: torch.Tensor, n_rows: int, n_tiles: int, bm: int, full_pos:
 
 
 def verify_build(seq: torch.Tensor, n_keys: int, n_drafts: int, bm: int, full_pos: torch.Tensor, x: torch.Tensor,
-                 x_draft: torch.Tensor):
+                 x_draft: torch.Tensor, out=None):
     """Flash-Verify forward inputs from per-sequence scalars (``seq`` int64
     [n, 8], see fdllm_verify_build) -> device (qpos, x_verify, mask bool
     [n * 2bm, 2bm], key slots, draft slots, logit rows, verify blocks int32
-    [n, 4], acceptance rows int64 [n, 4])."""
+    [n, 4], acceptance rows int64 [n, 4]); ``out`` = (qpos, x_verify, mask,
+    key slots, logit rows, verify blocks) to write into."""
     _check(seq, "seq", torch.int64, 2)
     _check(full_pos, "full_pos", torch.int64, 2)
     n, dev, r = seq.shape[0], seq.device, 2 * bm
     i64 = dict(dtype=torch.int64, device=dev)
-    qpos, xv = torch.empty(n * r, **i64), torch.empty(n * r, **i64)
-    mask = torch.empty(n * r, r, dtype=torch.bool, device=dev)
-    kpos, dslot, lidx = torch.empty(n_keys, **i64), torch.empty(n_drafts, **i64), torch.empty(n_drafts, **i64)
-    vblocks = torch.empty(n, 4, dtype=torch.int32, device=dev)
+    dslot = torch.empty(n_drafts, **i64)
+    if out is None:
+        qpos, xv = torch.empty(n * r, **i64), torch.empty(n * r, **i64)
+        mask = torch.empty(n * r, r, dtype=torch.bool, device=dev)
+        kpos, lidx = torch.empty(n_keys, **i64), torch.empty(n_drafts, **i64)
+        vblocks = torch.empty(n, 4, dtype=torch.int32, device=dev)
+    else:
+        qpos, xv, mask, kpos, lidx, vblocks = out
+        if (qpos.numel() != n * r or xv.numel() != n * r or tuple(mask.shape) != (n * r, r) or kpos.numel() != n_keys
+                or lidx.numel() != n_drafts or tuple(vblocks.shape) != (n, 4)):
+            raise ValueError("verify_build: output buffers of the wrong size")
     info2 = torch.empty(n, 4, **i64)
     call("fdllm_verify_build", ptr(seq), n, bm, full_pos.shape[1], x.numel(), ptr(full_pos), ptr(x), ptr(x_draft),
          ptr(qpos), ptr(xv), ptr(mask), ptr(kpos), ptr(dslot), ptr(lidx), ptr(vblocks), ptr(info2), _stream())
